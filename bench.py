@@ -1,0 +1,454 @@
+#!/usr/bin/env python
+"""Benchmark of the Flash-EKV CIM FFN hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload gpt_m_ffn]
+
+One step = forward + backward of one Physical FFN block (VoltageMapping ->
+CIMLinear -> CIMLinear -> ADC affine) on the workload's tokens, bf16 autocast
+around the block (the CIM path stays fp32), followed at N > 1 by the one
+gradient all-reduce of data-parallel training.  Metric: fwd+bwd cell-evals/s,
+one cell = one (token, input, output) triple of a CIM projection.
+Per-GPU work is fixed (weak scaling): every rank processes the full token
+count of the workload.
+
+Prints ONE JSON line (rank 0).  The reference arm (``--impl reference``) times
+the CPU restatement of the reference LUT path (oracle/) on the host cores on a
+bounded token sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "isa-_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+WORKLOADS = {
+    # Physical GPT-M FFN block, batch 32 x seq 1024, T = 4096
+    "gpt_m_ffn": dict(model="Physical GPT-M FFN block", d=384, hidden=1536, batch=32, seq=1024, lut=4096),
+    # Physical ViT-M FFN block, batch 128 x 65 tokens, T = 8192
+    "vit_m_ffn": dict(model="Physical ViT-M FFN block", d=256, hidden=1024, batch=128, seq=65, lut=8192),
+}
+
+OPS_FWD, OPS_BWD = 16, 24  # algorithmic FP32 lane-ops per cell (forward, fused backward)
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gpt_m_ffn")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=1024,
+                    help="tokens of the CPU baseline sample (our arm)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def cells_per_token(wl) -> int:
+    return 2 * wl["d"] * wl["hidden"]
+
+
+# ------------------------------------------------------------------ clocks --
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": num(rows[0][2]), "samples": len(rows), "reasons": reasons,
+                "power_w_max": max((num(r[3]) or 0.0) for r in rows)}
+
+
+# ------------------------------------------------------------- helpers ----
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return json.loads(p.read_text())
+    except (OSError, ValueError):
+        return {}
+
+
+def fp32_peak(dev) -> dict:
+    """FFMA lane-op throughput of this GPU: burst (best single launch) and
+    sustained (back-to-back launches for ~2 s, the regime of a long step)."""
+    import torch
+
+    from isa_b200 import _lib
+
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    sink = torch.zeros(1, device=dev)
+    blocks, iters = sms * 8, 4000
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        ops = _lib.fp32_probe(sink, iters, blocks)
+    best = float("inf")
+    for _ in range(5):
+        s.record()
+        ops = _lib.fp32_probe(sink, iters, blocks)
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    n = max(1, int(2000.0 / best))
+    s.record()
+    for _ in range(n):
+        _lib.fp32_probe(sink, iters, blocks)
+    e.record()
+    e.synchronize()
+    return {"burst": ops / (best * 1e-3), "sustained": n * ops / (s.elapsed_time(e) * 1e-3)}
+
+
+def make_ffn(wl, dev, seed=0):
+    import torch
+
+    from isa_b200 import make_flash_transistor_ekv_config
+    from isa_b200.operators.cim import PhysicalFFN
+
+    cfg = make_flash_transistor_ekv_config(default_lut_size=wl["lut"])
+    cfg["LUT_DELTA_SIZE"] = wl["lut"]
+    torch.manual_seed(seed)
+    return PhysicalFFN(wl["d"], wl["hidden"], cfg).to(dev), cfg
+
+
+def ffn_step(ffn, x, gseed, allreduce):
+    import torch
+
+    for p in ffn.parameters():
+        p.grad = None
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        z = ffn(x)
+    loss = (z.float() * gseed).sum()
+    loss.backward()
+    if allreduce:
+        from isa_b200.distributed import allreduce_gradients
+        allreduce_gradients(ffn.parameters())
+    return loss
+
+
+def time_kernels(ffn, cfg, x, dev, reps=5):
+    """CUDA-event time of one forward and one backward launch per projection
+    (the stream the library launches on is torch's current stream)."""
+    import torch
+
+    from isa_b200 import _lib
+    from isa_b200.approximations.delta_lut import get_packed_lut, lut_geometry
+
+    geo = lut_geometry(cfg)
+    lut = get_packed_lut(cfg, dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+    res = {}
+    with torch.no_grad():
+        x1 = x.reshape(-1, x.shape[-1]).float().clamp(0, 4).contiguous()
+        h = torch.empty(x1.shape[0], ffn.fc1.out_features, device=dev)
+        _lib.forward(x1, ffn.fc1.vth_pos, ffn.fc1.vth_neg, lut, geo.size, geo.delta_min_f32, geo.scale,
+                     float(cfg["V_sat"]), -4.0, 4.0, h)
+        h = (h * ffn.fc1.r_tia).clamp(-4, 4).contiguous()
+        for name, lin, xin in (("fc1", ffn.fc1, x1), ("fc2", ffn.fc2, h)):
+            m, k = xin.shape
+            o = lin.out_features
+            out = torch.empty(m, o, device=dev)
+            g = torch.randn(m, o, device=dev)
+            gx, gwp, gwn = torch.empty_like(xin), torch.empty_like(lin.vth_pos), torch.empty_like(lin.vth_neg)
+            ws = torch.empty(_lib.backward_workspace_bytes(m, k, o, geo.size), dtype=torch.uint8, device=dev)
+            t = {"fwd": [], "bwd": []}
+            for i in range(reps + 1):
+                for kind in ("fwd", "bwd"):
+                    flush.zero_()
+                    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s.record()
+                    if kind == "fwd":
+                        _lib.forward(xin, lin.vth_pos, lin.vth_neg, lut, geo.size, geo.delta_min_f32, geo.scale,
+                                     float(cfg["V_sat"]), -4.0, 4.0, out)
+                    else:
+                        _lib.backward(xin, lin.vth_pos, lin.vth_neg, g, lut, geo.size, geo.delta_min_f32,
+                                      geo.scale, float(cfg["V_sat"]), gx, gwp, gwn, ws)
+                    e.record()
+                    e.synchronize()
+                    if i > 0:
+                        t[kind].append(s.elapsed_time(e))
+            res[name] = {"cells": m * k * o, "fwd_ms": statistics.median(t["fwd"]),
+                         "bwd_ms": statistics.median(t["bwd"])}
+    return res
+
+
+def cpu_sample(wl, tokens, nthreads=0, seed=0):
+    """Oracle (CPU restatement of the reference LUT path) fwd+bwd of both
+    projections of the block on `tokens` tokens.  Returns (cells, seconds)."""
+    import numpy as np
+    import torch
+
+    from isa_b200 import make_flash_transistor_ekv_config
+    from isa_b200.approximations.delta_lut import build_lut_tables_cpu, lut_geometry
+    from isa_b200.operators.cim import CIMLinear
+    from oracle import oracle
+
+    cfg = make_flash_transistor_ekv_config(default_lut_size=wl["lut"])
+    cfg["LUT_DELTA_SIZE"] = wl["lut"]
+    geo = lut_geometry(cfg)
+    ti, td = (t.float().numpy() for t in build_lut_tables_cpu(cfg))
+    torch.manual_seed(seed)
+    fc1, fc2 = CIMLinear(wl["d"], wl["hidden"], cfg), CIMLinear(wl["hidden"], wl["d"], cfg)
+    rng = np.random.default_rng(seed)
+    x = np.clip(rng.standard_normal((tokens, wl["d"])), 0, 4).astype(np.float32)
+    args = (geo.delta_min_f32, geo.scale, float(cfg["V_sat"]))
+    w1 = (fc1.vth_pos.detach().numpy(), fc1.vth_neg.detach().numpy())
+    w2 = (fc2.vth_pos.detach().numpy(), fc2.vth_neg.detach().numpy())
+    g2 = rng.standard_normal((tokens, wl["d"])).astype(np.float32)
+    t0 = time.perf_counter()
+    h = oracle.forward(x, *w1, ti, *args, nthreads=nthreads)
+    h = np.clip(h * np.float32(1e5), -4, 4).astype(np.float32)
+    oracle.forward(h, *w2, ti, *args, nthreads=nthreads)
+    g1, _, _ = oracle.backward(h, *w2, g2, ti, td, *args, nthreads=nthreads)
+    oracle.backward(x, *w1, g1 * np.float32(1e5), ti, td, *args, nthreads=nthreads)
+    return tokens * cells_per_token(wl), time.perf_counter() - t0
+
+
+# ------------------------------------------------------------ our arm -----
+
+def run_ours(args, wl):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    ffn, cfg = make_ffn(wl, dev)
+    B, S, d = wl["batch"], wl["seq"], wl["d"]
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    x = torch.randn(B, S, d, device=dev, generator=gen)  # post-LayerNorm scale
+    gseed = torch.randn(B, S, d, device=dev, generator=gen)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+    allreduce = world > 1
+
+    for _ in range(max(args.warmup, 3)):
+        ffn_step(ffn, x, gseed, allreduce)
+    barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        barrier()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            ffn_step(ffn, x, gseed, allreduce)
+            ends[i].record()
+        barrier()
+    ms_rank = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    t = torch.tensor([ms_rank], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = float(t.item())
+    tokens = B * S
+    cells_step = tokens * cells_per_token(wl)
+    value = world * cells_step * args.steps / (ms_total * 1e-3)
+
+    # End to end through the public module API: the step's input from pinned
+    # host memory, the loss back to the host, every step.
+    x_host = x.cpu().pin_memory()
+    loss_host = torch.empty((), pin_memory=True)
+    for _ in range(2):
+        ffn_step(ffn, x_host.to(dev, non_blocking=True), gseed, allreduce)
+    barrier()
+    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        e_starts[i].record()
+        xd = x_host.to(dev, non_blocking=True)
+        loss = ffn_step(ffn, xd, gseed, allreduce)
+        loss_host.copy_(loss.detach(), non_blocking=True)
+        e_ends[i].record()
+    barrier()
+    e_ms = torch.tensor([sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends))], device=dev)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = world * cells_step * args.steps / (float(e_ms.item()) * 1e-3)
+
+    kern = time_kernels(ffn, cfg, x, dev) if rank == 0 else None
+    peak = fp32_peak(dev) if rank == 0 else None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle
+        c, sec = cpu_sample(wl, args.cpu_sample_tokens)
+        cpu = {"value": c / sec / 1e9, "unit": "Gcell-evals/s", "cores": oracle.max_threads(), "kind": "port",
+               "sample": f"{args.cpu_sample_tokens} tokens of the block (both projections, fwd+bwd), "
+                         f"oracle/cimekv_oracle.c with OpenMP, {sec:.1f} s"}
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        clk = clocks.summary()
+        # Dominant kernel: the one with the largest total time per step.
+        per = []
+        for name, k in kern.items():
+            per.append((k["fwd_ms"], f"{name}.fwd", k["cells"] * OPS_FWD))
+            per.append((k["bwd_ms"], f"{name}.bwd", k["cells"] * OPS_BWD))
+        dom_ms, dom_name, dom_ops = max(per)
+        pk = peak["sustained"]
+        achieved = dom_ops / (dom_ms * 1e-3)
+        traffic = None
+        tf = ROOT / "profiles" / "traffic.json"
+        if tf.exists():
+            try:
+                traffic = json.loads(tf.read_text()).get(args.workload, {}).get(dom_name)
+            except ValueError:
+                traffic = None
+        kernel_ms = sum(k["fwd_ms"] + k["bwd_ms"] for k in kern.values())
+        rec = {
+            "metric": "CIM-FFN fwd+bwd Gcell-evals/s",
+            "value": value / 1e9,
+            "unit": "Gcell-evals/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_total / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic: x ~ N(0,1) (post-LayerNorm scale), Vth ~ U(2.5 +- 0.107) (CIMLinear init), "
+                    "upstream grad ~ N(0,1)",
+            "config": {"workload": args.workload, "model": wl["model"], "global_batch": wl["batch"] * world,
+                       "seq_len": wl["seq"], "tokens_per_gpu": tokens, "d": wl["d"], "hidden": wl["hidden"],
+                       "lut_size": wl["lut"], "autocast": "bf16 (CIM path fp32)", "parallelism": f"dp{world}",
+                       "l2": "flushed (256 MiB write) before every timed step"},
+            "tokens_per_s": world * tokens * args.steps / (ms_total * 1e-3),
+            "e2e": {"value": e2e_value / 1e9, "unit": "Gcell-evals/s",
+                    "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+                    "d2h_bytes_per_step": loss_host.numel() * loss_host.element_size()},
+            "roofline": {"bound": "fp32_issue", "kernel": dom_name, "achieved": achieved / 1e12,
+                         "peak": pk / 1e12, "unit": "Tlane-op/s", "frac": achieved / pk, "traffic": traffic,
+                         "peak_source": "measured FFMA probe (cimekv_fp32_probe), sustained",
+                         "peak_burst": peak["burst"] / 1e12,
+                         "step_frac": value * (OPS_FWD + OPS_BWD) / pk,
+                         "kernel_share_of_step": kernel_ms / (ms_total / args.steps),
+                         "kernels_ms": kern,
+                         "ops_per_cell": {"fwd": OPS_FWD, "bwd": OPS_BWD},
+                         "hbm_peak_gbs": measured_peaks().get("hbm_gbs")},
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "gpu_launches": 6 * args.steps,
+            "impl": "ours",
+        }
+        print(json.dumps(rec), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------ reference arm -----
+
+def run_reference(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # rank 0 alone times the host CPU path
+    from oracle import oracle
+
+    tokens = 128  # bounded sample per step: ~1 s of CPU work on 8 cores
+    for _ in range(max(args.warmup, 1)):
+        cpu_sample(wl, tokens)
+    total_c, total_s = 0, 0.0
+    for i in range(args.steps):
+        c, s = cpu_sample(wl, tokens, seed=i)
+        total_c += c
+        total_s += s
+    v = total_c / total_s / 1e9
+    cores = oracle.max_threads()
+    rec = {
+        "metric": "CIM-FFN fwd+bwd Gcell-evals/s", "value": v, "unit": "Gcell-evals/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_s * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic, same distributions as our arm",
+        "config": {"workload": args.workload, "model": wl["model"], "tokens_per_step_sample": tokens,
+                   "d": wl["d"], "hidden": wl["hidden"], "lut_size": wl["lut"], "parallelism": "host CPU"},
+        "impl": "reference",
+        "cpu_baseline": {"value": v, "unit": "Gcell-evals/s", "cores": cores, "kind": "port",
+                         "sample": f"{tokens} tokens of the block per step (both projections, fwd+bwd): "
+                                   "CPU restatement of the reference LUT path, oracle/cimekv_oracle.c, OpenMP"},
+        "e2e": {"value": v, "unit": "Gcell-evals/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(rec), flush=True)
+
+
+def main():
+    args = parse()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,119 @@
+/*
+ * cimekv.h — C ABI of the B200 (sm_100a) Flash-EKV CIMLinear LUT operator.
+ *
+ * Plain pointers and sizes only; every tensor argument is a DEVICE pointer to
+ * contiguous row-major fp32 data (bf16 bit patterns as uint16 for the raw
+ * tables) on the device that is current when the call is made.  `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream).  Calls are
+ * asynchronous with respect to the host and return a status code; the text of
+ * the last error on the calling thread is available from cimekv_last_error().
+ * The library allocates no device memory: outputs and the backward workspace
+ * are owned by the caller.
+ *
+ * Shapes follow the reference operator: x[M,K] (tokens x in_features),
+ * wpos/wneg[O,K] (threshold voltages, out_features x in_features),
+ * out/grad_out[M,O].
+ */
+#ifndef CIMEKV_H
+#define CIMEKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    CIMEKV_OK = 0,
+    CIMEKV_EINVAL_SHAPE = 1,    /* bad sizes, null or misaligned pointers  */
+    CIMEKV_ELUT_TOO_LARGE = 2,  /* table or tile does not fit shared memory */
+    CIMEKV_ECUDA = 3,           /* a CUDA runtime call or launch failed     */
+    CIMEKV_EWORKSPACE = 4       /* backward workspace too small             */
+};
+
+/* Largest LUT_DELTA_SIZE the kernels accept. */
+#define CIMEKV_MAX_LUT_SIZE 16384
+
+/* Version of the ABI (bumped on any signature or layout change). */
+int cimekv_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* cimekv_last_error(void);
+
+/* Bytes of the packed device table for a LUT of `table_size` entries. */
+size_t cimekv_lut_bytes(int table_size);
+
+/*
+ * Pack the two bf16 tables (table_i = I(dV), table_ddelta = dI/ddV, each
+ * `table_size` entries, the layout returned by the reference builder
+ * get_ekv_lut_tables, src/isa/approximations/delta_lut.py:41-63) into the
+ * layout the kernels stage in shared memory.  `lut` receives
+ * cimekv_lut_bytes(table_size) bytes and must be 16-byte aligned.
+ */
+int cimekv_lut_pack(const uint16_t* table_i, const uint16_t* table_ddelta,
+                    int table_size, void* lut, void* stream);
+
+/*
+ * Forward: out[m,o] = clamp(sum_k (L(x[m,k]-wpos[o,k]) - L(x[m,k]-wneg[o,k]))
+ *                           / (1 + x[m,k]/v_sat), out_min, out_max)
+ * with L the linear interpolation of table_i at
+ *   f = clamp((dV - delta_min) * delta_scale, 0, T-1).
+ * Replaces the reference Triton _forward_kernel launched by
+ * LUTTritonEKVMatmulFn.forward (src/isa/kernels/transformer_ffn/
+ * ekv_lut_triton.py:37-62,151-157); delta_scale = float((T-1)/(dmax-dmin)).
+ */
+int cimekv_forward(const float* x, const float* wpos, const float* wneg,
+                   const void* lut, int M, int K, int O, int table_size,
+                   float delta_min, float delta_scale, float v_sat,
+                   float out_min, float out_max, float* out, void* stream);
+
+/*
+ * Workspace bytes cimekv_backward needs for these sizes on the current device.
+ */
+size_t cimekv_backward_workspace_bytes(int M, int K, int O, int table_size);
+
+/*
+ * Fused backward, one pass over the (m,o,k) cells:
+ *   grad_x[m,k]    = sum_o g[m,o] * ((dp-dn)/d - (bp-bn)/(v_sat d^2))
+ *   grad_wpos[o,k] = sum_m g[m,o] * (-dp/d)
+ *   grad_wneg[o,k] = sum_m g[m,o] * ( dn/d)
+ * with d = 1 + x/v_sat, b* / d* the interpolated table_i / table_ddelta at
+ * dV = x - w*.  Replaces the reference's two CUDA kernels
+ * ekv_grad_x_shared_kernel and ekv_grad_w_shared_kernel
+ * (src/isa/kernels/transformer_ffn/cuda/ekv_cuda.cu:193-341, host wrappers
+ * :433-574, bound as grad_x_shared / grad_w_shared in cuda/binding.cpp:56-62).
+ * grad_x may be NULL (no input gradient); grad_wpos and grad_wneg may both be
+ * NULL (no threshold gradient).  The result is deterministic.
+ */
+int cimekv_backward(const float* x, const float* wpos, const float* wneg,
+                    const float* grad_out, const void* lut,
+                    int M, int K, int O, int table_size,
+                    float delta_min, float delta_scale, float v_sat,
+                    float* grad_x, float* grad_wpos, float* grad_wneg,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Index selection of one lookup, for parity tests: for each dV in delta[n],
+ * writes the table entry i0 the kernels use and the interpolation weight a,
+ * computed by the same device code as the forward and backward
+ * (reference rule: ekv_lut_triton.py:26-31, ekv_cuda.cu:29-32).
+ */
+int cimekv_lut_index(const float* delta, int n, int table_size,
+                     float delta_min, float delta_scale,
+                     int32_t* index, float* alpha, void* stream);
+
+/*
+ * Measurement utility with no counterpart in the reference: launches `blocks`
+ * CTAs of 256 threads that each issue iters*128 independent FFMAs, and
+ * reports the lane-ops issued in *lane_ops.  Timed with events by the caller,
+ * it gives the FP32 CUDA-core peak that the operator's roofline is quoted
+ * against.  `sink` is a device float that is (almost) never written.
+ */
+int cimekv_fp32_probe(float* sink, int iters, int blocks, long long* lane_ops, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CIMEKV_H */

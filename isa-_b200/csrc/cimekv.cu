@@ -1,0 +1,865 @@
+// cimekv.cu — Flash-EKV CIMLinear LUT operator for B200 (sm_100a).
+//
+// One (token m, input k, output o) "cell" evaluates the EKV branch current of
+// both transistors of a differential pair through a 1-D table over
+// dV = x[m,k] - vth[o,k] with linear interpolation, divides by the velocity
+// saturation term d = 1 + x/V_sat and sums over k (forward) or produces the
+// two gradients dX (sum over o) and dVth (sum over m) (backward).
+//
+// The work is a "non-dense" contraction: every cell needs a data-dependent
+// table lookup, so it runs on the FP32/INT CUDA-core pipes with the tables held
+// in shared memory; the tensor cores cannot express it.  Design points:
+//  * the table index is computed exactly like the reference
+//    (f = (fl(x-w) - dmin) * scale, clamp to [0,T-1], i0 = trunc(f),
+//    a = f - i0; ekv_lut_triton.py:26-31, ekv_cuda.cu:29-32) but truncation
+//    uses the IEEE round-toward-zero add of 2^23, whose result bits hold i0 and
+//    double as the shared-memory address (no F2I/I2F conversions);
+//  * the clamp is skipped for every tile whose x and Vth ranges provably keep
+//    f inside the table (checked with the same monotone fp32 ops per tile);
+//  * tables are packed as bf16 pairs (the reference tables are bf16-exact,
+//    delta_lut.py:35), so one 32-bit shared load returns both interpolation
+//    nodes of the forward and one 64-bit load the four nodes of the backward;
+//  * the backward computes dX and dVth from the same lookups in one pass; dX
+//    is reduced in registers over all outputs, dVth over the tile's tokens in
+//    shared memory and over token splits by a deterministic second kernel.
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "cimekv.h"
+
+namespace {
+
+// ---------------------------------------------------------------- errors --
+
+thread_local char g_last_error[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        return set_error(CIMEKV_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+    }
+    return CIMEKV_OK;
+}
+
+// --------------------------------------------------------- device limits --
+
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mutex;
+int g_sm_count[kMaxDevices] = {0};
+int g_smem_optin[kMaxDevices] = {0};
+bool g_attr_set[kMaxDevices][4] = {};
+
+int current_device(int* dev) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return set_error(CIMEKV_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    if (*dev < 0 || *dev >= kMaxDevices) return set_error(CIMEKV_ECUDA, "device ordinal %d out of range", *dev);
+    return CIMEKV_OK;
+}
+
+int device_limits(int dev, int* sms, int* smem_optin) {
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    if (g_sm_count[dev] == 0) {
+        cudaError_t e1 = cudaDeviceGetAttribute(&g_sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+        cudaError_t e2 = cudaDeviceGetAttribute(&g_smem_optin[dev], cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e1 != cudaSuccess || e2 != cudaSuccess) {
+            g_sm_count[dev] = 0;
+            return set_error(CIMEKV_ECUDA, "cudaDeviceGetAttribute failed");
+        }
+    }
+    *sms = g_sm_count[dev];
+    *smem_optin = g_smem_optin[dev];
+    return CIMEKV_OK;
+}
+
+template <typename Kernel>
+int allow_smem(int dev, int slot, Kernel kernel, int smem_optin) {
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    if (!g_attr_set[dev][slot]) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin);
+        if (e != cudaSuccess) {
+            return set_error(CIMEKV_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        }
+        g_attr_set[dev][slot] = true;
+    }
+    return CIMEKV_OK;
+}
+
+// ------------------------------------------------------ table + indexing --
+
+constexpr float kTwo23 = 8388608.0f;       // 2^23
+constexpr uint32_t kTwo23Bits = 0x4B000000u;  // bit pattern of 2^23
+
+// Packed table layout in global memory:
+//   [0, fwd_bytes)           uint32 fwd[T]:  lo16 = bf16(I[j]), hi16 = bf16(I[j+1])
+//   [fwd_bytes, +8T)         uint2  bwd[T]:  .x = {I[j], I[j+1]}, .y = {dI[j], dI[j+1]}
+// with j+1 clamped to T-1, so entry T-1 interpolates to I[T-1] for any a.
+__host__ __device__ inline size_t fwd_table_bytes(int T) { return ((size_t)T * 4 + 15) & ~(size_t)15; }
+__host__ __device__ inline size_t bwd_table_bytes(int T) { return (size_t)T * 8; }
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// Table coordinate of one lookup: f = (fl(x - w) - dmin) * scale, each step
+// rounded to fp32 (never contracted), optionally clamped to [0, T-1].
+template <bool kClamp>
+__device__ __forceinline__ float lut_coord(float x, float w, float dmin, float scale, float fmax_) {
+    const float d = __fsub_rn(x, w);
+    float f = __fmul_rn(__fsub_rn(d, dmin), scale);
+    if (kClamp) f = fminf(fmaxf(f, 0.0f), fmax_);
+    return f;
+}
+
+// For 0 <= f < 2^23: t = f + 2^23 rounded toward zero is 2^23 + trunc(f), so
+// its bit pattern is kTwo23Bits + i0; a = f - i0 is exact.
+__device__ __forceinline__ void lut_split(float f, uint32_t& bits, float& a) {
+    const float t = __fadd_rz(f, kTwo23);
+    bits = __float_as_uint(t);
+    a = __fsub_rn(f, __fsub_rn(t, kTwo23));
+}
+
+__device__ __forceinline__ uint32_t smem_u32addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
+// fp32 tile-range test: true when every cell of a tile whose x lie in
+// [xmin, xmax] and thresholds in [wmin, wmax] has 0 <= f < T, i.e. the clamp is
+// a no-op.  Valid because fp32 subtraction and multiplication by a positive
+// constant are monotone under round-to-nearest.
+__device__ __forceinline__ bool tile_in_table(float xmin, float xmax, float wmin, float wmax,
+                                              bool has_nan, float dmin, float scale, int T) {
+    const float flo = lut_coord<false>(xmin, wmax, dmin, scale, 0.0f);
+    const float fhi = lut_coord<false>(xmax, wmin, dmin, scale, 0.0f);
+    return !has_nan && flo >= 0.0f && fhi < static_cast<float>(T);
+}
+
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, s));
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, s));
+    return v;
+}
+
+// Block-wide min/max of (a_min, a_max, b_min, b_max) and OR of a NaN flag.
+// `red` holds >= 8 float4 + 8 ints after it.  Contains __syncthreads().
+__device__ __forceinline__ void block_range4(float4 v, bool nan, float4* red, int* red_nan,
+                                             float4& out, bool& out_nan) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    v.x = warp_min(v.x);
+    v.y = warp_max(v.y);
+    v.z = warp_min(v.z);
+    v.w = warp_max(v.w);
+    const bool any_nan = __any_sync(0xffffffffu, nan);
+    if (lane == 0) {
+        red[warp] = v;
+        red_nan[warp] = any_nan ? 1 : 0;
+    }
+    __syncthreads();
+    float4 r = red[0];
+    int n = red_nan[0];
+    for (int w = 1; w < nwarps; ++w) {
+        const float4 q = red[w];
+        r.x = fminf(r.x, q.x);
+        r.y = fmaxf(r.y, q.y);
+        r.z = fminf(r.z, q.z);
+        r.w = fmaxf(r.w, q.w);
+        n |= red_nan[w];
+    }
+    out = r;
+    out_nan = n != 0;
+}
+
+// -------------------------------------------------------------- packing --
+
+__global__ void lut_pack_kernel(const uint16_t* __restrict__ ti, const uint16_t* __restrict__ td, int T,
+                                uint32_t* __restrict__ fwd, uint2* __restrict__ bwd, int fwd_words) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < fwd_words; j += gridDim.x * blockDim.x) {
+        if (j < T) {
+            const int j1 = j + 1 < T ? j + 1 : T - 1;
+            const uint32_t i0 = ti[j], i1 = ti[j1], d0 = td[j], d1 = td[j1];
+            fwd[j] = i0 | (i1 << 16);
+            bwd[j] = make_uint2(i0 | (i1 << 16), d0 | (d1 << 16));
+        } else {
+            fwd[j] = 0u;  // alignment padding, never indexed
+        }
+    }
+}
+
+__global__ void lut_index_kernel(const float* __restrict__ delta, int n, int T, float dmin, float scale,
+                                 int32_t* __restrict__ index, float* __restrict__ alpha) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    // dV is handed in directly: same coordinate as lut_coord with x = dV, w = 0
+    // (fl(dV - 0) = dV).
+    const float f = lut_coord<true>(delta[i], 0.0f, dmin, scale, static_cast<float>(T - 1));
+    uint32_t bits;
+    float a;
+    lut_split(f, bits, a);
+    index[i] = static_cast<int32_t>(bits - kTwo23Bits);
+    alpha[i] = a;
+}
+
+// -------------------------------------------------------------- forward --
+//
+// CTA tile: 64 tokens x 64 outputs, 256 threads.  Warp w owns tokens
+// [8w, 8w+8) of the tile; lane l owns outputs l and l+32.  The k dimension is
+// streamed in chunks of 16 through shared memory (x and 1/d transposed to
+// k-major so a warp reads its 8 tokens with two broadcast 128-bit loads), with
+// the next chunk prefetched into registers while the current one computes.
+// Persistent grid: each CTA stages the table once and walks a strided list of
+// tiles.
+
+constexpr int kFwdThreads = 256;
+constexpr int kFwdMT = 64;
+constexpr int kFwdOT = 64;
+constexpr int kFwdKC = 16;
+constexpr int kFwdLD = 68;  // padded row stride (floats) of the k-major tiles
+constexpr int kFwdStageFloats = 4 * kFwdKC * kFwdLD;
+constexpr int kFwdPerThread = kFwdMT * kFwdKC / kFwdThreads;  // 4 elements of each tile
+
+struct FwdParams {
+    const float* x;
+    const float* wp;
+    const float* wn;
+    const uint32_t* lut;
+    float* out;
+    int M, K, O, T;
+    float dmin, scale, vsat, out_min, out_max;
+};
+
+template <bool kClamp>
+__device__ __forceinline__ void fwd_chunk(const float* __restrict__ xs, const float* __restrict__ is,
+                                          const float* __restrict__ ps, const float* __restrict__ ns,
+                                          uint32_t tab_base, float dmin, float scale, float fmax_,
+                                          float (&acc)[8][2]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll 2
+    for (int kk = 0; kk < kFwdKC; ++kk) {
+        const float4 xa = *reinterpret_cast<const float4*>(xs + kk * kFwdLD + warp * 8);
+        const float4 xb = *reinterpret_cast<const float4*>(xs + kk * kFwdLD + warp * 8 + 4);
+        const float4 ia = *reinterpret_cast<const float4*>(is + kk * kFwdLD + warp * 8);
+        const float4 ib = *reinterpret_cast<const float4*>(is + kk * kFwdLD + warp * 8 + 4);
+        const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        const float iv[8] = {ia.x, ia.y, ia.z, ia.w, ib.x, ib.y, ib.z, ib.w};
+        const float wp[2] = {ps[kk * kFwdLD + lane], ps[kk * kFwdLD + lane + 32]};
+        const float wn[2] = {ns[kk * kFwdLD + lane], ns[kk * kFwdLD + lane + 32]};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                uint32_t bp_, bn_;
+                float ap, an;
+                lut_split(lut_coord<kClamp>(xv[i], wp[j], dmin, scale, fmax_), bp_, ap);
+                lut_split(lut_coord<kClamp>(xv[i], wn[j], dmin, scale, fmax_), bn_, an);
+                const uint32_t ep = lds32(tab_base + (bp_ << 2));
+                const uint32_t en = lds32(tab_base + (bn_ << 2));
+                const float p0 = bf16_lo(ep), n0 = bf16_lo(en);
+                const float vp = fmaf(ap, bf16_hi(ep) - p0, p0);
+                const float vn = fmaf(an, bf16_hi(en) - n0, n0);
+                acc[i][j] = fmaf(vp - vn, iv[i], acc[i][j]);
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kFwdThreads, 2) fwd_kernel(FwdParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int T = p.T;
+    uint32_t* tab = reinterpret_cast<uint32_t*>(smem);
+    float* stage = reinterpret_cast<float*>(smem + fwd_table_bytes(T));
+    float* xs = stage;
+    float* is = stage + kFwdKC * kFwdLD;
+    float* ps = stage + 2 * kFwdKC * kFwdLD;
+    float* ns = stage + 3 * kFwdKC * kFwdLD;
+    float4* red = reinterpret_cast<float4*>(stage + kFwdStageFloats);
+    int* red_nan = reinterpret_cast<int*>(red + 8);
+
+    {   // stage the table once per CTA
+        const uint4* src = reinterpret_cast<const uint4*>(p.lut);
+        uint4* dst = reinterpret_cast<uint4*>(tab);
+        const int n16 = static_cast<int>(fwd_table_bytes(T) / 16);
+        for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src[i];
+    }
+    // Biased shared address: tab_base + (bits << 2) = &tab[bits - kTwo23Bits].
+    const uint32_t tab_base = smem_u32addr(tab) - (kTwo23Bits << 2);
+    const float fmax_ = static_cast<float>(T - 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_m = (p.M + kFwdMT - 1) / kFwdMT;
+    const int tiles_o = (p.O + kFwdOT - 1) / kFwdOT;
+    const int ntiles = tiles_m * tiles_o;
+    const int nchunks = (p.K + kFwdKC - 1) / kFwdKC;
+
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int m0 = (tile / tiles_o) * kFwdMT;
+        const int o0 = (tile % tiles_o) * kFwdOT;
+        float acc[8][2];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = 0.0f;
+
+        // Register prefetch of one chunk: element e = tid + 256 r of a 64x16 tile
+        // is (row e>>4, col e&15); rows are tokens for x, outputs for w.
+        float rx[kFwdPerThread], rp[kFwdPerThread], rn[kFwdPerThread];
+        auto load_chunk = [&](int k0) {
+#pragma unroll
+            for (int r = 0; r < kFwdPerThread; ++r) {
+                const int e = threadIdx.x + kFwdThreads * r;
+                const int row = e >> 4, k = k0 + (e & 15);
+                const bool kin = k < p.K;
+                const int gm = m0 + row, go = o0 + row;
+                rx[r] = (kin && gm < p.M) ? __ldg(p.x + (int64_t)gm * p.K + k) : 0.0f;
+                rp[r] = (kin && go < p.O) ? __ldg(p.wp + (int64_t)go * p.K + k) : 0.0f;
+                rn[r] = (kin && go < p.O) ? __ldg(p.wn + (int64_t)go * p.K + k) : 0.0f;
+            }
+        };
+        if (nchunks > 0) load_chunk(0);
+        for (int c = 0; c < nchunks; ++c) {
+            __syncthreads();  // previous chunk's readers are done with the stage
+            float4 rng = make_float4(INFINITY, -INFINITY, INFINITY, -INFINITY);
+            bool nan = false;
+#pragma unroll
+            for (int r = 0; r < kFwdPerThread; ++r) {
+                const int e = threadIdx.x + kFwdThreads * r;
+                const int row = e >> 4, kk = e & 15;
+                const int k = c * kFwdKC + kk;
+                const bool valid = k < p.K && m0 + row < p.M;
+                const float xv = rx[r];
+                xs[kk * kFwdLD + row] = xv;
+                is[kk * kFwdLD + row] = valid ? __frcp_rn(__fadd_rn(1.0f, __fdiv_rn(xv, p.vsat))) : 0.0f;
+                ps[kk * kFwdLD + row] = rp[r];
+                ns[kk * kFwdLD + row] = rn[r];
+                rng.x = fminf(rng.x, xv);
+                rng.y = fmaxf(rng.y, xv);
+                rng.z = fminf(rng.z, fminf(rp[r], rn[r]));
+                rng.w = fmaxf(rng.w, fmaxf(rp[r], rn[r]));
+                nan |= (xv != xv) | (rp[r] != rp[r]) | (rn[r] != rn[r]);
+            }
+            float4 tr;
+            bool tnan;
+            block_range4(rng, nan, red, red_nan, tr, tnan);  // includes the barrier
+            if (c + 1 < nchunks) load_chunk((c + 1) * kFwdKC);
+            if (tile_in_table(tr.x, tr.y, tr.z, tr.w, tnan, p.dmin, p.scale, T)) {
+                fwd_chunk<false>(xs, is, ps, ns, tab_base, p.dmin, p.scale, fmax_, acc);
+            } else {
+                fwd_chunk<true>(xs, is, ps, ns, tab_base, p.dmin, p.scale, fmax_, acc);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int m = m0 + warp * 8 + i;
+            if (m >= p.M) continue;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int o = o0 + lane + 32 * j;
+                if (o < p.O) {
+                    p.out[(int64_t)m * p.O + o] = fminf(fmaxf(acc[i][j], p.out_min), p.out_max);
+                }
+            }
+        }
+    }
+}
+
+size_t fwd_smem_bytes(int T) {
+    return fwd_table_bytes(T) + (size_t)kFwdStageFloats * 4 + 8 * sizeof(float4) + 8 * sizeof(int);
+}
+
+// ------------------------------------------------------------- backward --
+//
+// CTA = 4 inputs (k0..k0+3) x one token split; 256 threads.  For each 64-token
+// tile of the split, warp w owns tokens [8w, 8w+8) and lane l walks outputs
+// o = 32c + l.  Per thread and chunk c: 8 tokens x 4 inputs = 32 cells.
+//   * dX[m,k] accumulates in registers over all o of the lane, then one
+//     32-lane transpose-reduce per tile leaves lane l holding dX of
+//     (token l/4, input l%4);
+//   * dVth partials (sum over the thread's 8 tokens) are summed over the 8
+//     warps through shared memory into a per-CTA accumulator dW[2][O][4]
+//     that lives for the whole split; at the end it goes to the workspace
+//     slice of this split, and bwd_reduce_kernel sums the splits in a fixed
+//     order (deterministic).
+
+constexpr int kBwdThreads = 256;
+constexpr int kBwdMT = 64;
+constexpr int kBwdKT = 4;
+constexpr int kBwdTok = 8;  // tokens per thread
+
+struct BwdParams {
+    const float* x;
+    const float* wp;
+    const float* wn;
+    const float* g;
+    const uint2* lut;
+    float* grad_x;
+    float* part;  // [nsplit][2][O][K]
+    int M, K, O, T;
+    int tiles_m, nsplit;
+    float dmin, scale, vsat;
+};
+
+size_t bwd_smem_bytes(int T, int O) {
+    const int opad = (O + 31) / 32 * 32;
+    return bwd_table_bytes(T)                        // table
+           + (size_t)2 * opad * kBwdKT * 4           // dW accumulator
+           + (size_t)3 * kBwdMT * 16                 // x, 1/d, 1/(vsat d^2) per token (float4 over k)
+           + (size_t)2 * 8 * 8 * 32 * 4              // double-buffered cross-warp dW exchange
+           + 8 * sizeof(float4) + 8 * sizeof(int);   // range reduction
+}
+
+template <bool kClamp>
+__device__ __forceinline__ void bwd_chunk(const float4* __restrict__ X4, const float4* __restrict__ I4,
+                                          const float4* __restrict__ T4, const float (&g)[kBwdTok],
+                                          const float (&wp)[kBwdKT], const float (&wn)[kBwdKT],
+                                          uint32_t tab_base, float dmin, float scale, float fmax_,
+                                          float (&dx)[kBwdTok * kBwdKT], float (&ap)[kBwdKT],
+                                          float (&an)[kBwdKT]) {
+    const int warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int i = 0; i < kBwdTok; ++i) {
+        const float4 x4 = X4[warp * kBwdTok + i];
+        const float4 i4 = I4[warp * kBwdTok + i];
+        const float4 t4 = T4[warp * kBwdTok + i];
+        const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+        const float iv[4] = {i4.x, i4.y, i4.z, i4.w};
+        const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+        const float gi = g[i];
+#pragma unroll
+        for (int kk = 0; kk < kBwdKT; ++kk) {
+            uint32_t bp_, bn_;
+            float alp, aln;
+            lut_split(lut_coord<kClamp>(xv[kk], wp[kk], dmin, scale, fmax_), bp_, alp);
+            lut_split(lut_coord<kClamp>(xv[kk], wn[kk], dmin, scale, fmax_), bn_, aln);
+            const uint2 ep = lds64(tab_base + (bp_ << 3));
+            const uint2 en = lds64(tab_base + (bn_ << 3));
+            const float pb0 = bf16_lo(ep.x), pd0 = bf16_lo(ep.y);
+            const float nb0 = bf16_lo(en.x), nd0 = bf16_lo(en.y);
+            const float pb = fmaf(alp, bf16_hi(ep.x) - pb0, pb0);
+            const float pd = fmaf(alp, bf16_hi(ep.y) - pd0, pd0);
+            const float nb = fmaf(aln, bf16_hi(en.x) - nb0, nb0);
+            const float nd = fmaf(aln, bf16_hi(en.y) - nd0, nd0);
+            const float deriv = (pd - nd) * iv[kk] - (pb - nb) * tv[kk];
+            dx[i * kBwdKT + kk] = fmaf(gi, deriv, dx[i * kBwdKT + kk]);
+            const float gd = gi * iv[kk];
+            ap[kk] = fmaf(gd, pd, ap[kk]);
+            an[kk] = fmaf(gd, nd, an[kk]);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int T = p.T;
+    const int opad = (p.O + 31) / 32 * 32;
+    uint2* tab = reinterpret_cast<uint2*>(smem);
+    float* dWs = reinterpret_cast<float*>(smem + bwd_table_bytes(T));  // [2][opad][4]
+    float4* X4 = reinterpret_cast<float4*>(dWs + 2 * opad * kBwdKT);
+    float4* I4 = X4 + kBwdMT;
+    float4* T4 = I4 + kBwdMT;
+    float* xch = reinterpret_cast<float*>(T4 + kBwdMT);  // [2][8 warps][8 vals][32 lanes]
+    float4* red = reinterpret_cast<float4*>(xch + 2 * 8 * 8 * 32);
+    int* red_nan = reinterpret_cast<int*>(red + 8);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int k0 = blockIdx.x * kBwdKT;
+    const int split = blockIdx.y;
+    const int tile_lo = (int)((int64_t)split * p.tiles_m / p.nsplit);
+    const int tile_hi = (int)((int64_t)(split + 1) * p.tiles_m / p.nsplit);
+
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(p.lut);
+        uint4* dst = reinterpret_cast<uint4*>(tab);
+        const int n16 = static_cast<int>(bwd_table_bytes(T) / 16);
+        for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src[i];
+        if ((T & 1) && threadIdx.x == 0) tab[T - 1] = p.lut[T - 1];
+        for (int i = threadIdx.x; i < 2 * opad * kBwdKT; i += blockDim.x) dWs[i] = 0.0f;
+    }
+    const uint32_t tab_base = smem_u32addr(tab) - (kTwo23Bits << 3);
+    const float fmax_ = static_cast<float>(T - 1);
+
+    // Threshold range of this CTA's inputs over all outputs (pads count as 0).
+    float4 wr;
+    bool wnan;
+    {
+        float4 v = make_float4(INFINITY, -INFINITY, INFINITY, -INFINITY);
+        bool nan = false;
+        for (int e = threadIdx.x; e < opad * kBwdKT; e += blockDim.x) {
+            const int o = e >> 2, k = k0 + (e & 3);
+            const bool valid = o < p.O && k < p.K;
+            const float a = valid ? __ldg(p.wp + (int64_t)o * p.K + k) : 0.0f;
+            const float b = valid ? __ldg(p.wn + (int64_t)o * p.K + k) : 0.0f;
+            v.z = fminf(v.z, fminf(a, b));
+            v.w = fmaxf(v.w, fmaxf(a, b));
+            nan |= (a != a) | (b != b);
+        }
+        block_range4(v, nan, red, red_nan, wr, wnan);
+    }
+
+    const int nchunks = (p.O + 31) / 32;
+    int xbuf = 0;
+    for (int tile = tile_lo; tile < tile_hi; ++tile) {
+        const int m0 = tile * kBwdMT;
+        __syncthreads();  // previous tile's readers of X4/I4/T4 and red are done
+        float xval;
+        {
+            const int t = threadIdx.x >> 2, kk = threadIdx.x & 3;
+            const int m = m0 + t, k = k0 + kk;
+            const bool valid = m < p.M && k < p.K;
+            xval = valid ? __ldg(p.x + (int64_t)m * p.K + k) : 0.0f;
+            const float d = __fadd_rn(1.0f, __fdiv_rn(xval, p.vsat));
+            reinterpret_cast<float*>(X4)[threadIdx.x] = xval;
+            reinterpret_cast<float*>(I4)[threadIdx.x] = valid ? __fdiv_rn(1.0f, d) : 0.0f;
+            reinterpret_cast<float*>(T4)[threadIdx.x] =
+                valid ? __fdiv_rn(1.0f, __fmul_rn(__fmul_rn(p.vsat, d), d)) : 0.0f;
+        }
+        float4 xr;
+        bool xnan;
+        block_range4(make_float4(xval, xval, INFINITY, -INFINITY), xval != xval, red, red_nan, xr, xnan);
+        const bool fast = tile_in_table(xr.x, xr.y, wr.z, wr.w, xnan || wnan, p.dmin, p.scale, T);
+
+        float dx[kBwdTok * kBwdKT];
+#pragma unroll
+        for (int i = 0; i < kBwdTok * kBwdKT; ++i) dx[i] = 0.0f;
+
+        // Register prefetch of chunk operands: g for the 8 tokens, thresholds
+        // of (o, k0..k0+3).
+        float gn[kBwdTok], wpn[kBwdKT], wnn[kBwdKT];
+        auto load_chunk = [&](int c) {
+            const int o = c * 32 + lane;
+            const bool oin = o < p.O;
+#pragma unroll
+            for (int i = 0; i < kBwdTok; ++i) {
+                const int m = m0 + warp * kBwdTok + i;
+                gn[i] = (oin && m < p.M) ? __ldg(p.g + (int64_t)m * p.O + o) : 0.0f;
+            }
+#pragma unroll
+            for (int kk = 0; kk < kBwdKT; ++kk) {
+                const bool valid = oin && k0 + kk < p.K;
+                wpn[kk] = valid ? __ldg(p.wp + (int64_t)o * p.K + k0 + kk) : 0.0f;
+                wnn[kk] = valid ? __ldg(p.wn + (int64_t)o * p.K + k0 + kk) : 0.0f;
+            }
+        };
+        if (nchunks > 0) load_chunk(0);
+        for (int c = 0; c < nchunks; ++c) {
+            float g[kBwdTok], wp[kBwdKT], wn[kBwdKT];
+#pragma unroll
+            for (int i = 0; i < kBwdTok; ++i) g[i] = gn[i];
+#pragma unroll
+            for (int kk = 0; kk < kBwdKT; ++kk) {
+                wp[kk] = wpn[kk];
+                wn[kk] = wnn[kk];
+            }
+            if (c + 1 < nchunks) load_chunk(c + 1);
+            float ap[kBwdKT] = {0.f, 0.f, 0.f, 0.f}, an[kBwdKT] = {0.f, 0.f, 0.f, 0.f};
+            if (fast) {
+                bwd_chunk<false>(X4, I4, T4, g, wp, wn, tab_base, p.dmin, p.scale, fmax_, dx, ap, an);
+            } else {
+                bwd_chunk<true>(X4, I4, T4, g, wp, wn, tab_base, p.dmin, p.scale, fmax_, dx, ap, an);
+            }
+            // Cross-warp sum of the dVth partials, accumulated into dWs.
+            float* xb = xch + xbuf * (8 * 8 * 32);
+#pragma unroll
+            for (int kk = 0; kk < kBwdKT; ++kk) {
+                xb[(warp * 8 + kk) * 32 + lane] = ap[kk];
+                xb[(warp * 8 + 4 + kk) * 32 + lane] = an[kk];
+            }
+            __syncthreads();
+            {
+                const int v = threadIdx.x >> 5;  // value slot 0..7 (p k0..3, n k0..3)
+                float s = 0.0f;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) s += xb[(w * 8 + v) * 32 + lane];
+                const int o = c * 32 + lane;
+                dWs[((v >> 2) * opad + o) * kBwdKT + (v & 3)] += s;
+            }
+            xbuf ^= 1;
+        }
+        // 32-lane transpose-reduce of dx: afterwards lane l holds the full sum
+        // of element l = (token l/4, input l%4).
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) {
+            const bool upper = (lane & s) != 0;
+#pragma unroll
+            for (int j = 0; j < s; ++j) {
+                const float send = upper ? dx[j] : dx[j + s];
+                const float keep = upper ? dx[j + s] : dx[j];
+                dx[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+            }
+        }
+        if (p.grad_x != nullptr) {
+            const int m = m0 + warp * kBwdTok + (lane >> 2), k = k0 + (lane & 3);
+            if (m < p.M && k < p.K) p.grad_x[(int64_t)m * p.K + k] = dx[0];
+        }
+    }
+    __syncthreads();
+    if (p.part != nullptr) {
+        for (int e = threadIdx.x; e < 2 * p.O * kBwdKT; e += blockDim.x) {
+            const int br = e / (p.O * kBwdKT);
+            const int rem = e - br * p.O * kBwdKT;
+            const int o = rem >> 2, kk = rem & 3;
+            if (k0 + kk < p.K) {
+                p.part[(((int64_t)split * 2 + br) * p.O + o) * p.K + k0 + kk] = dWs[(br * opad + o) * kBwdKT + kk];
+            }
+        }
+    }
+}
+
+// grad_wpos = -sum_s part[s][0], grad_wneg = +sum_s part[s][1], fixed order.
+__global__ void bwd_reduce_kernel(const float* __restrict__ part, int nsplit, int64_t n,
+                                  float* __restrict__ gwp, float* __restrict__ gwn) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        float sp = 0.0f, sn = 0.0f;
+        for (int s = 0; s < nsplit; ++s) {
+            sp += part[((int64_t)s * 2 + 0) * n + i];
+            sn += part[((int64_t)s * 2 + 1) * n + i];
+        }
+        gwp[i] = -sp;
+        gwn[i] = sn;
+    }
+}
+
+__global__ void fill_zero_kernel(float* __restrict__ p, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        p[i] = 0.0f;
+}
+
+// Token splits of the backward: enough CTAs to fill the GPU in whole waves.
+struct BwdPlan {
+    int kblocks, tiles_m, nsplit;
+    size_t smem, workspace;
+};
+
+int plan_backward(int M, int K, int O, int T, BwdPlan* plan) {
+    int dev, sms, optin;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    if ((rc = device_limits(dev, &sms, &optin))) return rc;
+    plan->kblocks = (K + kBwdKT - 1) / kBwdKT;
+    plan->tiles_m = (M + kBwdMT - 1) / kBwdMT;
+    plan->smem = bwd_smem_bytes(T, O);
+    if (plan->smem > (size_t)optin) {
+        return set_error(CIMEKV_ELUT_TOO_LARGE,
+                         "backward needs %zu B of shared memory (LUT size %d, out_features %d); device allows %d",
+                         plan->smem, T, O, optin);
+    }
+    // Resident CTAs per SM: 2 by registers, fewer if shared memory is short.
+    const size_t per_sm = 228 * 1024;
+    int resident = (int)(per_sm / (plan->smem + 1024));
+    if (resident > 2) resident = 2;
+    if (resident < 1) resident = 1;
+    const int slots = sms * resident;
+    int best = 1;
+    double best_cost = 1e30;
+    const int max_split = plan->tiles_m < 64 ? (plan->tiles_m > 0 ? plan->tiles_m : 1) : 64;
+    for (int s = 1; s <= max_split; ++s) {
+        const long total = (long)plan->kblocks * s;
+        const long waves = (total + slots - 1) / slots;
+        // time ~ waves * (tiles per split); small penalty per split for the
+        // workspace traffic of the reduction.
+        const double tiles_per_split = (double)((plan->tiles_m + s - 1) / s);
+        const double cost = (double)waves * tiles_per_split * (double)O + 4.0 * s * (double)O / 64.0;
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = s;
+        }
+    }
+    plan->nsplit = best;
+    plan->workspace = (size_t)best * 2 * (size_t)O * (size_t)K * sizeof(float);
+    return CIMEKV_OK;
+}
+
+int check_lut_size(int T) {
+    if (T < 2 || T > CIMEKV_MAX_LUT_SIZE) {
+        return set_error(CIMEKV_ELUT_TOO_LARGE, "LUT size %d outside [2, %d]", T, CIMEKV_MAX_LUT_SIZE);
+    }
+    return CIMEKV_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+// ================================================================ C ABI ==
+
+extern "C" {
+
+int cimekv_abi_version(void) { return 1; }
+
+const char* cimekv_last_error(void) { return g_last_error; }
+
+size_t cimekv_lut_bytes(int table_size) {
+    if (table_size < 2 || table_size > CIMEKV_MAX_LUT_SIZE) return 0;
+    return fwd_table_bytes(table_size) + bwd_table_bytes(table_size);
+}
+
+int cimekv_lut_pack(const uint16_t* table_i, const uint16_t* table_ddelta, int table_size, void* lut,
+                    void* stream) {
+    g_last_error[0] = '\0';
+    int rc = check_lut_size(table_size);
+    if (rc) return rc;
+    if (!table_i || !table_ddelta || !lut) return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
+    if (!aligned16(lut)) return set_error(CIMEKV_EINVAL_SHAPE, "lut must be 16-byte aligned");
+    const int fwd_words = (int)(fwd_table_bytes(table_size) / 4);
+    uint32_t* fwd = static_cast<uint32_t*>(lut);
+    uint2* bwd = reinterpret_cast<uint2*>(static_cast<unsigned char*>(lut) + fwd_table_bytes(table_size));
+    lut_pack_kernel<<<(fwd_words + 255) / 256, 256, 0, (cudaStream_t)stream>>>(table_i, table_ddelta, table_size,
+                                                                                fwd, bwd, fwd_words);
+    return check_launch("lut_pack_kernel");
+}
+
+int cimekv_forward(const float* x, const float* wpos, const float* wneg, const void* lut, int M, int K, int O,
+                   int table_size, float delta_min, float delta_scale, float v_sat, float out_min, float out_max,
+                   float* out, void* stream) {
+    g_last_error[0] = '\0';
+    int rc = check_lut_size(table_size);
+    if (rc) return rc;
+    if (M < 0 || K < 0 || O < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative size M=%d K=%d O=%d", M, K, O);
+    if (M == 0 || O == 0) return CIMEKV_OK;
+    if (!lut || !out || (K > 0 && (!x || !wpos || !wneg)))
+        return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
+    if (!aligned16(lut)) return set_error(CIMEKV_EINVAL_SHAPE, "lut must be 16-byte aligned");
+    if (!(delta_scale > 0.0f)) return set_error(CIMEKV_EINVAL_SHAPE, "delta_scale must be > 0");
+    int dev, sms, optin;
+    if ((rc = current_device(&dev))) return rc;
+    if ((rc = device_limits(dev, &sms, &optin))) return rc;
+    const size_t smem = fwd_smem_bytes(table_size);
+    if (smem > (size_t)optin) return set_error(CIMEKV_ELUT_TOO_LARGE, "forward needs %zu B shared memory", smem);
+    if ((rc = allow_smem(dev, 0, fwd_kernel, optin))) return rc;
+    FwdParams p;
+    p.x = x;
+    p.wp = wpos;
+    p.wn = wneg;
+    p.lut = static_cast<const uint32_t*>(lut);
+    p.out = out;
+    p.M = M;
+    p.K = K;
+    p.O = O;
+    p.T = table_size;
+    p.dmin = delta_min;
+    p.scale = delta_scale;
+    p.vsat = v_sat;
+    p.out_min = out_min;
+    p.out_max = out_max;
+    const long ntiles = (long)((M + kFwdMT - 1) / kFwdMT) * ((O + kFwdOT - 1) / kFwdOT);
+    int resident = (int)((228 * 1024) / (smem + 1024));
+    if (resident > 2) resident = 2;
+    if (resident < 1) resident = 1;
+    long grid = (long)sms * resident;
+    if (grid > ntiles) grid = ntiles;
+    fwd_kernel<<<(unsigned)grid, kFwdThreads, smem, (cudaStream_t)stream>>>(p);
+    return check_launch("fwd_kernel");
+}
+
+size_t cimekv_backward_workspace_bytes(int M, int K, int O, int table_size) {
+    if (M <= 0 || K <= 0 || O <= 0 || check_lut_size(table_size)) return 0;
+    BwdPlan plan;
+    if (plan_backward(M, K, O, table_size, &plan)) return 0;
+    return plan.workspace;
+}
+
+int cimekv_backward(const float* x, const float* wpos, const float* wneg, const float* grad_out, const void* lut,
+                    int M, int K, int O, int table_size, float delta_min, float delta_scale, float v_sat,
+                    float* grad_x, float* grad_wpos, float* grad_wneg, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+    g_last_error[0] = '\0';
+    int rc = check_lut_size(table_size);
+    if (rc) return rc;
+    if (M < 0 || K < 0 || O < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative size M=%d K=%d O=%d", M, K, O);
+    if ((grad_wpos == nullptr) != (grad_wneg == nullptr))
+        return set_error(CIMEKV_EINVAL_SHAPE, "grad_wpos and grad_wneg must both be given or both be NULL");
+    const bool want_w = grad_wpos != nullptr;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (K == 0) return CIMEKV_OK;
+    if (M == 0 || O == 0) {
+        // Empty sums: gradients are zero.
+        if (want_w && O > 0) {
+            fill_zero_kernel<<<64, 256, 0, s>>>(grad_wpos, (int64_t)O * K);
+            fill_zero_kernel<<<64, 256, 0, s>>>(grad_wneg, (int64_t)O * K);
+        }
+        if (grad_x && M > 0) fill_zero_kernel<<<64, 256, 0, s>>>(grad_x, (int64_t)M * K);
+        return check_launch("fill_zero_kernel");
+    }
+    if (!grad_x && !want_w) return CIMEKV_OK;
+    if (!x || !wpos || !wneg || !grad_out || !lut) return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
+    if (!aligned16(lut)) return set_error(CIMEKV_EINVAL_SHAPE, "lut must be 16-byte aligned");
+    if (!(delta_scale > 0.0f)) return set_error(CIMEKV_EINVAL_SHAPE, "delta_scale must be > 0");
+    BwdPlan plan;
+    if ((rc = plan_backward(M, K, O, table_size, &plan))) return rc;
+    if (want_w) {
+        if (!workspace || workspace_bytes < plan.workspace)
+            return set_error(CIMEKV_EWORKSPACE, "backward workspace needs %zu B, got %zu B", plan.workspace,
+                             workspace_bytes);
+        if (!aligned16(workspace)) return set_error(CIMEKV_EINVAL_SHAPE, "workspace must be 16-byte aligned");
+    }
+    int dev, sms, optin;
+    if ((rc = current_device(&dev))) return rc;
+    if ((rc = device_limits(dev, &sms, &optin))) return rc;
+    if ((rc = allow_smem(dev, 1, bwd_kernel, optin))) return rc;
+    BwdParams p;
+    p.x = x;
+    p.wp = wpos;
+    p.wn = wneg;
+    p.g = grad_out;
+    p.lut = reinterpret_cast<const uint2*>(static_cast<const unsigned char*>(lut) + fwd_table_bytes(table_size));
+    p.grad_x = grad_x;
+    p.part = want_w ? static_cast<float*>(workspace) : nullptr;
+    p.M = M;
+    p.K = K;
+    p.O = O;
+    p.T = table_size;
+    p.tiles_m = plan.tiles_m;
+    p.nsplit = plan.nsplit;
+    p.dmin = delta_min;
+    p.scale = delta_scale;
+    p.vsat = v_sat;
+    dim3 grid(plan.kblocks, plan.nsplit);
+    bwd_kernel<<<grid, kBwdThreads, plan.smem, s>>>(p);
+    if ((rc = check_launch("bwd_kernel"))) return rc;
+    if (want_w) {
+        const int64_t n = (int64_t)O * K;
+        int blocks = (int)((n + 255) / 256);
+        if (blocks > sms * 8) blocks = sms * 8;
+        bwd_reduce_kernel<<<blocks, 256, 0, s>>>(p.part, plan.nsplit, n, grad_wpos, grad_wneg);
+        if ((rc = check_launch("bwd_reduce_kernel"))) return rc;
+    }
+    return CIMEKV_OK;
+}
+
+int cimekv_lut_index(const float* delta, int n, int table_size, float delta_min, float delta_scale, int32_t* index,
+                     float* alpha, void* stream) {
+    g_last_error[0] = '\0';
+    int rc = check_lut_size(table_size);
+    if (rc) return rc;
+    if (n < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative n");
+    if (n == 0) return CIMEKV_OK;
+    if (!delta || !index || !alpha) return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
+    lut_index_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(delta, n, table_size, delta_min,
+                                                                         delta_scale, index, alpha);
+    return check_launch("lut_index_kernel");
+}
+
+}  // extern "C"

@@ -1,0 +1,147 @@
+"""ctypes binding of ``libcimekv.so`` (the C ABI in ``include/cimekv.h``).
+
+Every wrapper takes torch tensors, checks them the way the reference's
+``check_float_cuda_contiguous`` does (``ekv_cuda.cu:343-347``: CUDA, float32,
+contiguous) and raises ``RuntimeError`` carrying ``cimekv_last_error()`` when
+the library reports a failure.  There is no fallback: without the library the
+import of this module fails.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+_LIB_PATH = Path(os.environ.get("CIMEKV_LIB", Path(__file__).resolve().parent / "_lib" / "libcimekv.so"))
+
+_c_int, _c_float, _c_size, _vp = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
+
+# name -> (restype, argtypes); mirrors include/cimekv.h
+SIGNATURES = {
+    "cimekv_abi_version": (_c_int, []),
+    "cimekv_last_error": (ctypes.c_char_p, []),
+    "cimekv_lut_bytes": (_c_size, [_c_int]),
+    "cimekv_lut_pack": (_c_int, [_vp, _vp, _c_int, _vp, _vp]),
+    "cimekv_forward": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+                                _c_float, _c_float, _c_float, _c_float, _c_float, _vp, _vp]),
+    "cimekv_backward_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, _c_int]),
+    "cimekv_backward": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+                                 _c_float, _c_float, _c_float, _vp, _vp, _vp, _vp, _c_size, _vp]),
+    "cimekv_lut_index": (_c_int, [_vp, _c_int, _c_int, _c_float, _c_float, _vp, _vp, _vp]),
+    "cimekv_fp32_probe": (_c_int, [_vp, _c_int, _c_int, ctypes.POINTER(ctypes.c_longlong), _vp]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once (raises if it has not been built)."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not _LIB_PATH.exists():
+                raise RuntimeError(
+                    f"libcimekv.so not found at {_LIB_PATH}; build it with `python -m isa_b200.build` "
+                    "(there is no CPU fallback for the CIM operator)"
+                )
+            lib = ctypes.CDLL(str(_LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def library_path() -> Path:
+    return _LIB_PATH
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().cimekv_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what} failed (status {rc}): {msg}")
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def check_float_cuda_contiguous(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if t.dtype != torch.float32:
+        raise RuntimeError(f"{name} must be float32")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def lut_bytes(table_size: int) -> int:
+    n = load().cimekv_lut_bytes(int(table_size))
+    if n == 0:
+        raise RuntimeError(f"unsupported LUT size {table_size}")
+    return int(n)
+
+
+def lut_pack(table_i: torch.Tensor, table_ddelta: torch.Tensor, table_size: int, packed: torch.Tensor,
+             stream=None) -> None:
+    for t, n in ((table_i, "table_i"), (table_ddelta, "table_ddelta")):
+        if not t.is_cuda or t.dtype != torch.bfloat16 or not t.is_contiguous() or t.numel() != table_size:
+            raise RuntimeError(f"{n} must be a contiguous CUDA bf16 tensor of {table_size} entries")
+    rc = load().cimekv_lut_pack(_ptr(table_i), _ptr(table_ddelta), int(table_size), _ptr(packed), _stream(stream))
+    _check(rc, "cimekv_lut_pack")
+
+
+def forward(x, wpos, wneg, lut, table_size, delta_min, delta_scale, v_sat, out_min, out_max, out,
+            stream=None) -> None:
+    m, k = x.shape
+    o = wpos.shape[0]
+    rc = load().cimekv_forward(_ptr(x), _ptr(wpos), _ptr(wneg), _ptr(lut), m, k, o, int(table_size),
+                               delta_min, delta_scale, v_sat, out_min, out_max, _ptr(out), _stream(stream))
+    _check(rc, "cimekv_forward")
+
+
+def backward_workspace_bytes(m: int, k: int, o: int, table_size: int) -> int:
+    return int(load().cimekv_backward_workspace_bytes(int(m), int(k), int(o), int(table_size)))
+
+
+def backward(x, wpos, wneg, grad_out, lut, table_size, delta_min, delta_scale, v_sat,
+             grad_x, grad_wpos, grad_wneg, workspace, stream=None) -> None:
+    m, k = x.shape
+    o = wpos.shape[0]
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = load().cimekv_backward(_ptr(x), _ptr(wpos), _ptr(wneg), _ptr(grad_out), _ptr(lut), m, k, o,
+                                int(table_size), delta_min, delta_scale, v_sat,
+                                _ptr(grad_x), _ptr(grad_wpos), _ptr(grad_wneg),
+                                _ptr(workspace), ws_bytes, _stream(stream))
+    _check(rc, "cimekv_backward")
+
+
+def lut_index(delta: torch.Tensor, table_size: int, delta_min: float, delta_scale: float,
+              stream=None) -> tuple[torch.Tensor, torch.Tensor]:
+    check_float_cuda_contiguous(delta, "delta")
+    index = torch.empty(delta.shape, dtype=torch.int32, device=delta.device)
+    alpha = torch.empty(delta.shape, dtype=torch.float32, device=delta.device)
+    rc = load().cimekv_lut_index(_ptr(delta), delta.numel(), int(table_size), delta_min, delta_scale,
+                                 _ptr(index), _ptr(alpha), _stream(stream))
+    _check(rc, "cimekv_lut_index")
+    return index, alpha
+
+
+def fp32_probe(sink: torch.Tensor, iters: int, blocks: int, stream=None) -> int:
+    """Launch the FFMA probe; returns the lane-ops it issues."""
+    ops = ctypes.c_longlong(0)
+    rc = load().cimekv_fp32_probe(_ptr(sink), int(iters), int(blocks), ctypes.byref(ops), _stream(stream))
+    _check(rc, "cimekv_fp32_probe")
+    return int(ops.value)

@@ -1,0 +1,203 @@
+"""Parity of the sm_100a kernels (called through the C ABI) with the CPU oracle
+and with the reference's own outputs (golden vectors)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests._util import GOLDEN, GOLDEN_CASES, assert_close_scaled, bf16_bits_to_f32, geometry, load_golden
+
+pytestmark = pytest.mark.gpu
+
+CFG_V_SAT = 8.2624
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from isa_b200 import build
+    build.build_library()
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def pack(table_i_bits, table_dd_bits):
+    from isa_b200 import _lib
+    size = table_i_bits.size
+    ti = _dev(table_i_bits.view(np.int16)).view(torch.bfloat16)
+    td = _dev(table_dd_bits.view(np.int16)).view(torch.bfloat16)
+    lut = torch.empty(_lib.lut_bytes(size), dtype=torch.uint8, device="cuda")
+    _lib.lut_pack(ti, td, size, lut)
+    return lut
+
+
+def gpu_forward(x, wp, wn, lut, dmin, scale, size, v_sat=CFG_V_SAT, out_min=-4.0, out_max=4.0):
+    from isa_b200 import _lib
+    xd, pd, nd = _dev(x), _dev(wp), _dev(wn)
+    out = torch.empty((x.shape[0], wp.shape[0]), dtype=torch.float32, device="cuda")
+    _lib.forward(xd, pd, nd, lut, size, dmin, scale, v_sat, out_min, out_max, out)
+    return out.cpu().numpy()
+
+
+def gpu_backward(x, wp, wn, g, lut, dmin, scale, size, v_sat=CFG_V_SAT, need_x=True, need_w=True):
+    from isa_b200 import _lib
+    xd, pd, nd, gd = _dev(x), _dev(wp), _dev(wn), _dev(g)
+    m, k = x.shape
+    o = wp.shape[0]
+    gx = torch.full((m, k), float("nan"), device="cuda") if need_x else None
+    gwp = torch.full((o, k), float("nan"), device="cuda") if need_w else None
+    gwn = torch.full((o, k), float("nan"), device="cuda") if need_w else None
+    ws = None
+    if need_w:
+        ws = torch.empty(max(_lib.backward_workspace_bytes(m, k, o, size), 16), dtype=torch.uint8, device="cuda")
+    _lib.backward(xd, pd, nd, gd, lut, size, dmin, scale, v_sat, gx, gwp, gwn, ws)
+    return tuple(None if t is None else t.cpu().numpy() for t in (gx, gwp, gwn))
+
+
+def cfg_tables(size):
+    from isa_b200.approximations.delta_lut import build_lut_tables_cpu, lut_geometry
+    from isa_b200.device_models.config import make_flash_transistor_ekv_config
+    cfg = make_flash_transistor_ekv_config(default_lut_size=size)
+    cfg["LUT_DELTA_SIZE"] = size
+    ti, td = build_lut_tables_cpu(cfg)
+    geo = lut_geometry(cfg)
+    tib = ti.view(torch.int16).numpy().view(np.uint16)
+    tdb = td.view(torch.int16).numpy().view(np.uint16)
+    return tib, tdb, geo.delta_min_f32, geo.scale, size
+
+
+def check_all(x, wp, wn, g, tib, tdb, dmin, scale, size, rtol=1e-5, tag=""):
+    lut = pack(tib, tdb)
+    ti, td = bf16_bits_to_f32(tib), bf16_bits_to_f32(tdb)
+    out = gpu_forward(x, wp, wn, lut, dmin, scale, size)
+    ref_out, mag = oracle.forward(x, wp, wn, ti, dmin, scale, CFG_V_SAT, with_mag=True)
+    assert_close_scaled(out, ref_out, mag, rtol=rtol, what=f"{tag} forward")
+    gx, gwp, gwn = gpu_backward(x, wp, wn, g, lut, dmin, scale, size)
+    (rx, rwp, rwn), (mx, mwp, mwn) = oracle.backward(x, wp, wn, g, ti, td, dmin, scale, CFG_V_SAT, with_mag=True)
+    assert_close_scaled(gx, rx, mx, rtol=rtol, what=f"{tag} grad_x")
+    assert_close_scaled(gwp, rwp, mwp, rtol=rtol, what=f"{tag} grad_wpos")
+    assert_close_scaled(gwn, rwn, mwn, rtol=rtol, what=f"{tag} grad_wneg")
+    return out, (gx, gwp, gwn)
+
+
+@pytest.mark.parametrize("case", GOLDEN_CASES)
+def test_golden_cases(case):
+    gold = load_golden(case)
+    dmin, scale, size = geometry(gold)
+    out, (gx, gwp, gwn) = check_all(gold["x"], gold["wpos"], gold["wneg"], gold["grad_out"],
+                                    gold["table_i"], gold["table_ddelta"], dmin, scale, size, tag=case)
+    # and directly against the reference kernels' own outputs
+    ti, td = bf16_bits_to_f32(gold["table_i"]), bf16_bits_to_f32(gold["table_ddelta"])
+    _, mag = oracle.forward(gold["x"], gold["wpos"], gold["wneg"], ti, dmin, scale, CFG_V_SAT, with_mag=True)
+    assert_close_scaled(out, gold["out"], mag, what=f"{case} forward vs reference")
+    _, (mx, mwp, mwn) = oracle.backward(gold["x"], gold["wpos"], gold["wneg"], gold["grad_out"], ti, td,
+                                        dmin, scale, CFG_V_SAT, with_mag=True)
+    assert_close_scaled(gx, gold["grad_x"], mx, what=f"{case} grad_x vs reference")
+    assert_close_scaled(gwp, gold["grad_wpos"], mwp, what=f"{case} grad_wpos vs reference")
+    assert_close_scaled(gwn, gold["grad_wneg"], mwn, what=f"{case} grad_wneg vs reference")
+
+
+@pytest.mark.parametrize("size", [8192, 4096, 257, 2, 16384])
+def test_index_selection_bit_exact(size):
+    from isa_b200 import _lib
+    _, _, dmin, scale, _ = cfg_tables(size)
+    rng = np.random.default_rng(size)
+    step = 13.0 / (size - 1)
+    nodes = (-9.0 + step * rng.integers(0, size, 20000)).astype(np.float32)
+    delta = np.concatenate([
+        nodes, np.nextafter(nodes, np.float32(-np.inf)), np.nextafter(nodes, np.float32(np.inf)),
+        rng.uniform(-14, 9, 50000).astype(np.float32),
+        np.array([-9.0, 4.0, -1e30, 1e30, 0.0, -0.0], np.float32),
+    ]).astype(np.float32)
+    idx, alpha = _lib.lut_index(_dev(delta), size, dmin, scale)
+    ridx, ralpha = oracle.lut_index(delta, size, dmin, scale)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ridx)
+    np.testing.assert_array_equal(alpha.cpu().numpy(), ralpha)
+    if size in (8192, 4096):
+        with np.load(GOLDEN / "golden_index.npz") as z:
+            gd = z[f"delta_t{size}"]
+        gi, ga = _lib.lut_index(_dev(gd), size, dmin, scale)
+        ri, ra = oracle.lut_index(gd, size, dmin, scale)
+        np.testing.assert_array_equal(gi.cpu().numpy(), ri)
+        np.testing.assert_array_equal(ga.cpu().numpy(), ra)
+
+
+SHAPES = [
+    (1, 1, 1), (3, 5, 7), (64, 16, 64), (65, 17, 65), (130, 33, 97), (64, 200, 31), (200, 64, 300),
+    (257, 96, 130),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("size", [4096, 8192])
+def test_random_shapes_cim_init(shape, size):
+    m, k, o = shape
+    rng = np.random.default_rng(m * 1000 + k * 10 + o)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    wp = (2.5 + rng.uniform(-0.10712, 0.10712, (o, k))).astype(np.float32)
+    wn = (2.5 + rng.uniform(-0.10712, 0.10712, (o, k))).astype(np.float32)
+    g = rng.standard_normal((m, o)).astype(np.float32)
+    check_all(x, wp, wn, g, *cfg_tables(size), tag=f"{shape} T={size}")
+
+
+@pytest.mark.parametrize("dist", ["clamp_both", "voltage_mapped", "second_layer"])
+def test_input_distributions(dist):
+    rng = np.random.default_rng(7)
+    m, k, o = 150, 70, 90
+    if dist == "clamp_both":  # dV beyond both table ends: clamp path
+        x = rng.uniform(-9, 9, (m, k))
+        wp, wn = rng.uniform(-1, 6, (o, k)), rng.uniform(-1, 6, (o, k))
+    elif dist == "voltage_mapped":  # first projection: x in [0, 4], many at the clamp bounds
+        x = np.clip(rng.standard_normal((m, k)) * 2 + 2, 0, 4)
+        wp, wn = rng.uniform(0, 5, (o, k)), rng.uniform(0, 5, (o, k))
+    else:  # second projection: signed TIA output in [-4, 4]
+        x = np.clip(rng.standard_normal((m, k)) * 3, -4, 4)
+        wp, wn = 2.5 + rng.uniform(-0.2, 0.2, (o, k)), 2.5 + rng.uniform(-0.2, 0.2, (o, k))
+    g = rng.standard_normal((m, o))
+    f = np.float32
+    check_all(x.astype(f), wp.astype(f), wn.astype(f), g.astype(f), *cfg_tables(4096), tag=dist)
+
+
+def test_empty_sizes():
+    tib, tdb, dmin, scale, size = cfg_tables(4096)
+    lut = pack(tib, tdb)
+    rng = np.random.default_rng(0)
+    # K = 0: forward is clamp(0) = 0
+    out = gpu_forward(np.zeros((5, 0), np.float32), np.zeros((3, 0), np.float32), np.zeros((3, 0), np.float32),
+                      lut, dmin, scale, size)
+    np.testing.assert_array_equal(out, np.zeros((5, 3), np.float32))
+    # M = 0: threshold gradients are zero
+    x = np.zeros((0, 4), np.float32)
+    w = (2.5 + rng.uniform(-0.1, 0.1, (3, 4))).astype(np.float32)
+    gx, gwp, gwn = gpu_backward(x, w, w, np.zeros((0, 3), np.float32), lut, dmin, scale, size)
+    np.testing.assert_array_equal(gwp, 0)
+    np.testing.assert_array_equal(gwn, 0)
+    # O = 0: input gradient is zero
+    x = rng.standard_normal((6, 4)).astype(np.float32)
+    w0 = np.zeros((0, 4), np.float32)
+    gx, _, _ = gpu_backward(x, w0, w0, np.zeros((6, 0), np.float32), lut, dmin, scale, size)
+    np.testing.assert_array_equal(gx, 0)
+
+
+def test_partial_gradients_and_determinism():
+    tib, tdb, dmin, scale, size = cfg_tables(8192)
+    lut = pack(tib, tdb)
+    rng = np.random.default_rng(3)
+    m, k, o = 700, 48, 160
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    wp = (2.5 + rng.uniform(-0.1, 0.1, (o, k))).astype(np.float32)
+    wn = (2.5 + rng.uniform(-0.1, 0.1, (o, k))).astype(np.float32)
+    g = rng.standard_normal((m, o)).astype(np.float32)
+    full = gpu_backward(x, wp, wn, g, lut, dmin, scale, size)
+    again = gpu_backward(x, wp, wn, g, lut, dmin, scale, size)
+    for a, b in zip(full, again):
+        np.testing.assert_array_equal(a, b)  # deterministic reductions
+    only_x = gpu_backward(x, wp, wn, g, lut, dmin, scale, size, need_w=False)
+    only_w = gpu_backward(x, wp, wn, g, lut, dmin, scale, size, need_x=False)
+    np.testing.assert_array_equal(only_x[0], full[0])
+    np.testing.assert_array_equal(only_w[1], full[1])
+    np.testing.assert_array_equal(only_w[2], full[2])
