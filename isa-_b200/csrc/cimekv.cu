@@ -102,12 +102,12 @@ int allow_smem(int dev, int slot, Kernel kernel, int smem_optin) {
 constexpr float kTwo23 = 8388608.0f;       // 2^23
 constexpr uint32_t kTwo23Bits = 0x4B000000u;  // bit pattern of 2^23
 
-// Packed table layout in global memory:
-//   [0, fwd_bytes)           uint32 fwd[T]:  lo16 = bf16(I[j]), hi16 = bf16(I[j+1])
-//   [fwd_bytes, +8T)         uint2  bwd[T]:  .x = {I[j], I[j+1]}, .y = {dI[j], dI[j+1]}
-// with j+1 clamped to T-1, so entry T-1 interpolates to I[T-1] for any a.
+// Packed table layout in global memory (each part padded to 16 bytes):
+//   uint32 lut_i[T]:  lo16 = bf16(I[j]),  hi16 = bf16(I[j+1])
+//   uint32 lut_d[T]:  lo16 = bf16(dI[j]), hi16 = bf16(dI[j+1])
+// with j+1 clamped to T-1, so entry T-1 interpolates to its own value for any a.
 __host__ __device__ inline size_t fwd_table_bytes(int T) { return ((size_t)T * 4 + 15) & ~(size_t)15; }
-__host__ __device__ inline size_t bwd_table_bytes(int T) { return (size_t)T * 8; }
+
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
@@ -140,10 +140,76 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
     return v;
 }
 
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-    uint2 v;
-    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-    return v;
+// ---- packed fp32x2 arithmetic (sm_100: two fp32 ops per lane per issue) ----
+// The kernels pair two adjacent TOKENS (same output, input and branch), so
+// every pair op is the reference's scalar op applied twice with the same IEEE
+// rounding; only the issue count halves.
+typedef unsigned long long f32x2;
+
+__device__ __forceinline__ f32x2 pk2(float lo, float hi) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpk2(f32x2 v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f32x2 add2_rz(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("add.rz.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f32x2 sub2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+// Constants of the index math, broadcast into both halves of a pair.
+struct LutConsts {
+    f32x2 dmin2, scale2, two23;
+    float fmax_;
+    uint32_t tab_base;
+};
+
+// Table coordinate of two lookups (two tokens against one threshold):
+// returns the bit patterns of t = f + 2^23 (rz) per half and a = f - trunc(f).
+template <bool kClamp>
+__device__ __forceinline__ f32x2 lut_coord2(f32x2 xx, f32x2 ww, const LutConsts& c, uint32_t& b0, uint32_t& b1) {
+    f32x2 f = mul2(sub2(sub2(xx, ww), c.dmin2), c.scale2);
+    if (kClamp) {
+        float f0, f1;
+        unpk2(f, f0, f1);
+        f = pk2(fminf(fmaxf(f0, 0.0f), c.fmax_), fminf(fmaxf(f1, 0.0f), c.fmax_));
+    }
+    const f32x2 t = add2_rz(f, c.two23);
+    float t0, t1;
+    unpk2(t, t0, t1);
+    b0 = __float_as_uint(t0);
+    b1 = __float_as_uint(t1);
+    return sub2(f, sub2(t, c.two23));
+}
+
+// Forward lookup pair: interpolated I at two tokens.
+template <bool kClamp>
+__device__ __forceinline__ f32x2 lut_fwd2(f32x2 xx, f32x2 ww, const LutConsts& c) {
+    uint32_t b0, b1;
+    const f32x2 a = lut_coord2<kClamp>(xx, ww, c, b0, b1);
+    const uint32_t e0 = lds32(c.tab_base + (b0 << 2));
+    const uint32_t e1 = lds32(c.tab_base + (b1 << 2));
+    const f32x2 q0 = pk2(bf16_lo(e0), bf16_lo(e1));
+    const f32x2 q1 = pk2(bf16_hi(e0), bf16_hi(e1));
+    return fma2(a, sub2(q1, q0), q0);
 }
 
 // fp32 tile-range test: true when every cell of a tile whose x lie in
@@ -200,15 +266,15 @@ __device__ __forceinline__ void block_range4(float4 v, bool nan, float4* red, in
 // -------------------------------------------------------------- packing --
 
 __global__ void lut_pack_kernel(const uint16_t* __restrict__ ti, const uint16_t* __restrict__ td, int T,
-                                uint32_t* __restrict__ fwd, uint2* __restrict__ bwd, int fwd_words) {
-    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < fwd_words; j += gridDim.x * blockDim.x) {
+                                uint32_t* __restrict__ lut_i, uint32_t* __restrict__ lut_d, int words) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < words; j += gridDim.x * blockDim.x) {
         if (j < T) {
             const int j1 = j + 1 < T ? j + 1 : T - 1;
-            const uint32_t i0 = ti[j], i1 = ti[j1], d0 = td[j], d1 = td[j1];
-            fwd[j] = i0 | (i1 << 16);
-            bwd[j] = make_uint2(i0 | (i1 << 16), d0 | (d1 << 16));
+            lut_i[j] = (uint32_t)ti[j] | ((uint32_t)ti[j1] << 16);
+            lut_d[j] = (uint32_t)td[j] | ((uint32_t)td[j1] << 16);
         } else {
-            fwd[j] = 0u;  // alignment padding, never indexed
+            lut_i[j] = 0u;  // alignment padding, never indexed
+            lut_d[j] = 0u;
         }
     }
 }
@@ -258,8 +324,7 @@ struct FwdParams {
 template <bool kClamp>
 __device__ __forceinline__ void fwd_chunk(const float* __restrict__ xs, const float* __restrict__ is,
                                           const float* __restrict__ ps, const float* __restrict__ ns,
-                                          uint32_t tab_base, float dmin, float scale, float fmax_,
-                                          float (&acc)[8][2]) {
+                                          const LutConsts& c, f32x2 (&acc)[4][2]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll 2
     for (int kk = 0; kk < kFwdKC; ++kk) {
@@ -267,24 +332,22 @@ __device__ __forceinline__ void fwd_chunk(const float* __restrict__ xs, const fl
         const float4 xb = *reinterpret_cast<const float4*>(xs + kk * kFwdLD + warp * 8 + 4);
         const float4 ia = *reinterpret_cast<const float4*>(is + kk * kFwdLD + warp * 8);
         const float4 ib = *reinterpret_cast<const float4*>(is + kk * kFwdLD + warp * 8 + 4);
-        const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-        const float iv[8] = {ia.x, ia.y, ia.z, ia.w, ib.x, ib.y, ib.z, ib.w};
-        const float wp[2] = {ps[kk * kFwdLD + lane], ps[kk * kFwdLD + lane + 32]};
-        const float wn[2] = {ns[kk * kFwdLD + lane], ns[kk * kFwdLD + lane + 32]};
+        const f32x2 xx[4] = {pk2(xa.x, xa.y), pk2(xa.z, xa.w), pk2(xb.x, xb.y), pk2(xb.z, xb.w)};
+        const f32x2 iv[4] = {pk2(ia.x, ia.y), pk2(ia.z, ia.w), pk2(ib.x, ib.y), pk2(ib.z, ib.w)};
+        f32x2 wp[2], wn[2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int j = 0; j < 2; ++j) {
+            const float p = ps[kk * kFwdLD + lane + 32 * j], n = ns[kk * kFwdLD + lane + 32 * j];
+            wp[j] = pk2(p, p);
+            wn[j] = pk2(n, n);
+        }
+#pragma unroll
+        for (int ip = 0; ip < 4; ++ip) {
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                uint32_t bp_, bn_;
-                float ap, an;
-                lut_split(lut_coord<kClamp>(xv[i], wp[j], dmin, scale, fmax_), bp_, ap);
-                lut_split(lut_coord<kClamp>(xv[i], wn[j], dmin, scale, fmax_), bn_, an);
-                const uint32_t ep = lds32(tab_base + (bp_ << 2));
-                const uint32_t en = lds32(tab_base + (bn_ << 2));
-                const float p0 = bf16_lo(ep), n0 = bf16_lo(en);
-                const float vp = fmaf(ap, bf16_hi(ep) - p0, p0);
-                const float vn = fmaf(an, bf16_hi(en) - n0, n0);
-                acc[i][j] = fmaf(vp - vn, iv[i], acc[i][j]);
+                const f32x2 vp = lut_fwd2<kClamp>(xx[ip], wp[j], c);
+                const f32x2 vn = lut_fwd2<kClamp>(xx[ip], wn[j], c);
+                acc[ip][j] = fma2(sub2(vp, vn), iv[ip], acc[ip][j]);
             }
         }
     }
@@ -309,8 +372,12 @@ __global__ void __launch_bounds__(kFwdThreads, 2) fwd_kernel(FwdParams p) {
         for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src[i];
     }
     // Biased shared address: tab_base + (bits << 2) = &tab[bits - kTwo23Bits].
-    const uint32_t tab_base = smem_u32addr(tab) - (kTwo23Bits << 2);
-    const float fmax_ = static_cast<float>(T - 1);
+    LutConsts lc;
+    lc.tab_base = smem_u32addr(tab) - (kTwo23Bits << 2);
+    lc.fmax_ = static_cast<float>(T - 1);
+    lc.dmin2 = pk2(p.dmin, p.dmin);
+    lc.scale2 = pk2(p.scale, p.scale);
+    lc.two23 = pk2(kTwo23, kTwo23);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_m = (p.M + kFwdMT - 1) / kFwdMT;
     const int tiles_o = (p.O + kFwdOT - 1) / kFwdOT;
@@ -320,9 +387,9 @@ __global__ void __launch_bounds__(kFwdThreads, 2) fwd_kernel(FwdParams p) {
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const int m0 = (tile / tiles_o) * kFwdMT;
         const int o0 = (tile % tiles_o) * kFwdOT;
-        float acc[8][2];
+        f32x2 acc[4][2];  // [token pair][output]
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = 0.0f;
+        for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = pk2(0.0f, 0.0f);
 
         // Register prefetch of one chunk: element e = tid + 256 r of a 64x16 tile
         // is (row e>>4, col e&15); rows are tokens for x, outputs for w.
@@ -366,9 +433,9 @@ __global__ void __launch_bounds__(kFwdThreads, 2) fwd_kernel(FwdParams p) {
             block_range4(rng, nan, red, red_nan, tr, tnan);  // includes the barrier
             if (c + 1 < nchunks) load_chunk((c + 1) * kFwdKC);
             if (tile_in_table(tr.x, tr.y, tr.z, tr.w, tnan, p.dmin, p.scale, T)) {
-                fwd_chunk<false>(xs, is, ps, ns, tab_base, p.dmin, p.scale, fmax_, acc);
+                fwd_chunk<false>(xs, is, ps, ns, lc, acc);
             } else {
-                fwd_chunk<true>(xs, is, ps, ns, tab_base, p.dmin, p.scale, fmax_, acc);
+                fwd_chunk<true>(xs, is, ps, ns, lc, acc);
             }
         }
 #pragma unroll
@@ -378,8 +445,10 @@ __global__ void __launch_bounds__(kFwdThreads, 2) fwd_kernel(FwdParams p) {
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 const int o = o0 + lane + 32 * j;
+                float v0, v1;
+                unpk2(acc[i >> 1][j], v0, v1);
                 if (o < p.O) {
-                    p.out[(int64_t)m * p.O + o] = fminf(fmaxf(acc[i][j], p.out_min), p.out_max);
+                    p.out[(int64_t)m * p.O + o] = fminf(fmaxf((i & 1) ? v1 : v0, p.out_min), p.out_max);
                 }
             }
         }
@@ -393,8 +462,13 @@ size_t fwd_smem_bytes(int T) {
 // ------------------------------------------------------------- backward --
 //
 // CTA = 4 inputs (k0..k0+3) x one token split; 256 threads.  For each 64-token
-// tile of the split, warp w owns tokens [8w, 8w+8) and lane l walks outputs
-// o = 32c + l.  Per thread and chunk c: 8 tokens x 4 inputs = 32 cells.
+// tile of the split, warp w owns tokens [8w, 8w+8) (4 adjacent pairs) and lane
+// l walks outputs o = 32c + l.  Per thread and chunk c: 8 tokens x 4 inputs =
+// 32 cells.
+//   * the chunk's thresholds (32 outputs x 4 inputs x 2 branches) are staged
+//     once per CTA in a double-buffered shared tile, prefetched a chunk ahead;
+//   * the table is two 32-bit pair tables (I and dI/dV), the second at the
+//     compile-time offset kStride words, so one index feeds both loads;
 //   * dX[m,k] accumulates in registers over all o of the lane, then one
 //     32-lane transpose-reduce per tile leaves lane l holding dX of
 //     (token l/4, input l%4);
@@ -414,7 +488,8 @@ struct BwdParams {
     const float* wp;
     const float* wn;
     const float* g;
-    const uint2* lut;
+    const uint32_t* lut_i;   // [T] {I[j], I[j+1]}
+    const uint32_t* lut_d;   // [T] {dI[j], dI[j+1]}
     float* grad_x;
     float* part;  // [nsplit][2][O][K]
     int M, K, O, T;
@@ -422,65 +497,95 @@ struct BwdParams {
     float dmin, scale, vsat;
 };
 
+// Table stride (words) of the backward: the smallest supported size >= T.
+int bwd_stride(int T) { return T <= 4096 ? 4096 : (T <= 8192 ? 8192 : 16384); }
+
 size_t bwd_smem_bytes(int T, int O) {
     const int opad = (O + 31) / 32 * 32;
-    return bwd_table_bytes(T)                        // table
+    return (size_t)8 * bwd_stride(T)                 // I and dI/dV pair tables
            + (size_t)2 * opad * kBwdKT * 4           // dW accumulator
-           + (size_t)3 * kBwdMT * 16                 // x, 1/d, 1/(vsat d^2) per token (float4 over k)
+           + (size_t)3 * kBwdMT * kBwdKT * 4         // x, 1/d, -1/(vsat d^2): k-major [4][64]
+           + (size_t)2 * 32 * 8 * 4                  // double-buffered chunk thresholds
            + (size_t)2 * 8 * 8 * 32 * 4              // double-buffered cross-warp dW exchange
            + 8 * sizeof(float4) + 8 * sizeof(int);   // range reduction
 }
 
-template <bool kClamp>
-__device__ __forceinline__ void bwd_chunk(const float4* __restrict__ X4, const float4* __restrict__ I4,
-                                          const float4* __restrict__ T4, const float (&g)[kBwdTok],
-                                          const float (&wp)[kBwdKT], const float (&wn)[kBwdKT],
-                                          uint32_t tab_base, float dmin, float scale, float fmax_,
-                                          float (&dx)[kBwdTok * kBwdKT], float (&ap)[kBwdKT],
-                                          float (&an)[kBwdKT]) {
-    const int warp = threadIdx.x >> 5;
+template <int kOff>
+__device__ __forceinline__ uint32_t lds32_off(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(addr), "n"(kOff));
+    return v;
+}
+
+// Backward lookup pair: interpolated (I, dI/dV) at two tokens.
+template <bool kClamp, int kStride>
+__device__ __forceinline__ void lut_bwd2(f32x2 xx, f32x2 ww, const LutConsts& c, f32x2& base, f32x2& deriv) {
+    uint32_t b0, b1;
+    const f32x2 a = lut_coord2<kClamp>(xx, ww, c, b0, b1);
+    const uint32_t a0 = c.tab_base + (b0 << 2), a1 = c.tab_base + (b1 << 2);
+    const uint32_t i0 = lds32(a0), i1 = lds32(a1);
+    const uint32_t d0 = lds32_off<4 * kStride>(a0), d1 = lds32_off<4 * kStride>(a1);
+    const f32x2 qb0 = pk2(bf16_lo(i0), bf16_lo(i1));
+    const f32x2 qb1 = pk2(bf16_hi(i0), bf16_hi(i1));
+    const f32x2 qd0 = pk2(bf16_lo(d0), bf16_lo(d1));
+    const f32x2 qd1 = pk2(bf16_hi(d0), bf16_hi(d1));
+    base = fma2(a, sub2(qb1, qb0), qb0);
+    deriv = fma2(a, sub2(qd1, qd0), qd0);
+}
+
+// One chunk of 32 outputs for this thread's 8 tokens (4 pairs) x 4 inputs.
+// Xk/Ik/Nk: k-major [4][64] tiles of x, 1/d and -1/(v_sat d^2); ws: this
+// chunk's thresholds [32 outputs][p k0..3, n k0..3].
+template <bool kClamp, int kStride>
+__device__ __forceinline__ void bwd_chunk(const float* __restrict__ Xk, const float* __restrict__ Ik,
+                                          const float* __restrict__ Nk, const float* __restrict__ ws,
+                                          const float (&g)[kBwdTok], const LutConsts& c,
+                                          f32x2 (&dx)[4][kBwdKT], f32x2 (&ap)[kBwdKT], f32x2 (&an)[kBwdKT]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const f32x2 G[4] = {pk2(g[0], g[1]), pk2(g[2], g[3]), pk2(g[4], g[5]), pk2(g[6], g[7])};
+    const float4 wp4 = *reinterpret_cast<const float4*>(ws + lane * 8);
+    const float4 wn4 = *reinterpret_cast<const float4*>(ws + lane * 8 + 4);
+    const float wp[4] = {wp4.x, wp4.y, wp4.z, wp4.w};
+    const float wn[4] = {wn4.x, wn4.y, wn4.z, wn4.w};
 #pragma unroll
-    for (int i = 0; i < kBwdTok; ++i) {
-        const float4 x4 = X4[warp * kBwdTok + i];
-        const float4 i4 = I4[warp * kBwdTok + i];
-        const float4 t4 = T4[warp * kBwdTok + i];
-        const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
-        const float iv[4] = {i4.x, i4.y, i4.z, i4.w};
-        const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
-        const float gi = g[i];
+    for (int kk = 0; kk < kBwdKT; ++kk) {
+        const float* xr = Xk + kk * kBwdMT + warp * kBwdTok;
+        const float* ir = Ik + kk * kBwdMT + warp * kBwdTok;
+        const float* nr = Nk + kk * kBwdMT + warp * kBwdTok;
+        const float4 xa = *reinterpret_cast<const float4*>(xr), xb = *reinterpret_cast<const float4*>(xr + 4);
+        const float4 ia = *reinterpret_cast<const float4*>(ir), ib = *reinterpret_cast<const float4*>(ir + 4);
+        const float4 na = *reinterpret_cast<const float4*>(nr), nb4 = *reinterpret_cast<const float4*>(nr + 4);
+        const f32x2 X[4] = {pk2(xa.x, xa.y), pk2(xa.z, xa.w), pk2(xb.x, xb.y), pk2(xb.z, xb.w)};
+        const f32x2 IV[4] = {pk2(ia.x, ia.y), pk2(ia.z, ia.w), pk2(ib.x, ib.y), pk2(ib.z, ib.w)};
+        const f32x2 NT[4] = {pk2(na.x, na.y), pk2(na.z, na.w), pk2(nb4.x, nb4.y), pk2(nb4.z, nb4.w)};
+        const f32x2 WP = pk2(wp[kk], wp[kk]), WN = pk2(wn[kk], wn[kk]);
 #pragma unroll
-        for (int kk = 0; kk < kBwdKT; ++kk) {
-            uint32_t bp_, bn_;
-            float alp, aln;
-            lut_split(lut_coord<kClamp>(xv[kk], wp[kk], dmin, scale, fmax_), bp_, alp);
-            lut_split(lut_coord<kClamp>(xv[kk], wn[kk], dmin, scale, fmax_), bn_, aln);
-            const uint2 ep = lds64(tab_base + (bp_ << 3));
-            const uint2 en = lds64(tab_base + (bn_ << 3));
-            const float pb0 = bf16_lo(ep.x), pd0 = bf16_lo(ep.y);
-            const float nb0 = bf16_lo(en.x), nd0 = bf16_lo(en.y);
-            const float pb = fmaf(alp, bf16_hi(ep.x) - pb0, pb0);
-            const float pd = fmaf(alp, bf16_hi(ep.y) - pd0, pd0);
-            const float nb = fmaf(aln, bf16_hi(en.x) - nb0, nb0);
-            const float nd = fmaf(aln, bf16_hi(en.y) - nd0, nd0);
-            const float deriv = (pd - nd) * iv[kk] - (pb - nb) * tv[kk];
-            dx[i * kBwdKT + kk] = fmaf(gi, deriv, dx[i * kBwdKT + kk]);
-            const float gd = gi * iv[kk];
-            ap[kk] = fmaf(gd, pd, ap[kk]);
-            an[kk] = fmaf(gd, nd, an[kk]);
+        for (int ip = 0; ip < 4; ++ip) {
+            f32x2 pb, pd, nb, nd;
+            lut_bwd2<kClamp, kStride>(X[ip], WP, c, pb, pd);
+            lut_bwd2<kClamp, kStride>(X[ip], WN, c, nb, nd);
+            // d(I_diff/d)/dx = (dp - dn)/d - (bp - bn)/(v_sat d^2)
+            const f32x2 e = fma2(sub2(pb, nb), NT[ip], mul2(sub2(pd, nd), IV[ip]));
+            dx[ip][kk] = fma2(G[ip], e, dx[ip][kk]);
+            const f32x2 gi = mul2(G[ip], IV[ip]);
+            ap[kk] = fma2(gi, pd, ap[kk]);
+            an[kk] = fma2(gi, nd, an[kk]);
         }
     }
 }
 
+template <int kStride>
 __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int T = p.T;
     const int opad = (p.O + 31) / 32 * 32;
-    uint2* tab = reinterpret_cast<uint2*>(smem);
-    float* dWs = reinterpret_cast<float*>(smem + bwd_table_bytes(T));  // [2][opad][4]
-    float4* X4 = reinterpret_cast<float4*>(dWs + 2 * opad * kBwdKT);
-    float4* I4 = X4 + kBwdMT;
-    float4* T4 = I4 + kBwdMT;
-    float* xch = reinterpret_cast<float*>(T4 + kBwdMT);  // [2][8 warps][8 vals][32 lanes]
+    uint32_t* tab = reinterpret_cast<uint32_t*>(smem);                // [kStride] I pairs, [kStride] dI pairs
+    float* dWs = reinterpret_cast<float*>(smem + 8 * kStride);       // [2][opad][4]
+    float* Xk = dWs + 2 * opad * kBwdKT;  // [4][64] x
+    float* Ik = Xk + kBwdKT * kBwdMT;      // [4][64] 1/d
+    float* Nk = Ik + kBwdKT * kBwdMT;      // [4][64] -1/(v_sat d^2)
+    float* wsm = Nk + kBwdKT * kBwdMT;     // [2][32 outputs][8]
+    float* xch = wsm + 2 * 32 * 8;         // [2][8 warps][8 vals][32 lanes]
     float4* red = reinterpret_cast<float4*>(xch + 2 * 8 * 8 * 32);
     int* red_nan = reinterpret_cast<int*>(red + 8);
 
@@ -489,17 +594,32 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
     const int split = blockIdx.y;
     const int tile_lo = (int)((int64_t)split * p.tiles_m / p.nsplit);
     const int tile_hi = (int)((int64_t)(split + 1) * p.tiles_m / p.nsplit);
+    const int nchunks = (p.O + 31) / 32;
+
+    // Threshold staging: thread t fetches (output t/8 of the chunk, slot t%8),
+    // slot = branch*4 + input.
+    const int w_o = threadIdx.x >> 3, w_slot = threadIdx.x & 7;
+    const int w_k = k0 + (w_slot & 3);
+    const float* w_src = (w_slot < 4) ? p.wp : p.wn;
+    auto fetch_w = [&](int c) -> float {
+        const int o = c * 32 + w_o;
+        return (o < p.O && w_k < p.K) ? __ldg(w_src + (int64_t)o * p.K + w_k) : 0.0f;
+    };
 
     {
-        const uint4* src = reinterpret_cast<const uint4*>(p.lut);
-        uint4* dst = reinterpret_cast<uint4*>(tab);
-        const int n16 = static_cast<int>(bwd_table_bytes(T) / 16);
-        for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src[i];
-        if ((T & 1) && threadIdx.x == 0) tab[T - 1] = p.lut[T - 1];
+        for (int i = threadIdx.x; i < T; i += blockDim.x) {
+            tab[i] = p.lut_i[i];
+            tab[kStride + i] = p.lut_d[i];
+        }
         for (int i = threadIdx.x; i < 2 * opad * kBwdKT; i += blockDim.x) dWs[i] = 0.0f;
+        if (nchunks > 0) wsm[threadIdx.x] = fetch_w(0);  // chunk 0 into buffer 0
     }
-    const uint32_t tab_base = smem_u32addr(tab) - (kTwo23Bits << 3);
-    const float fmax_ = static_cast<float>(T - 1);
+    LutConsts lc;
+    lc.tab_base = smem_u32addr(tab) - (kTwo23Bits << 2);
+    lc.fmax_ = static_cast<float>(T - 1);
+    lc.dmin2 = pk2(p.dmin, p.dmin);
+    lc.scale2 = pk2(p.scale, p.scale);
+    lc.two23 = pk2(kTwo23, kTwo23);
 
     // Threshold range of this CTA's inputs over all outputs (pads count as 0).
     float4 wr;
@@ -516,14 +636,13 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
             v.w = fmaxf(v.w, fmaxf(a, b));
             nan |= (a != a) | (b != b);
         }
-        block_range4(v, nan, red, red_nan, wr, wnan);
+        block_range4(v, nan, red, red_nan, wr, wnan);  // barrier: table, dWs, wsm[0] visible
     }
 
-    const int nchunks = (p.O + 31) / 32;
-    int xbuf = 0;
+    int buf = 0;  // parity of the chunk-sized double buffers (thresholds, exchange)
     for (int tile = tile_lo; tile < tile_hi; ++tile) {
         const int m0 = tile * kBwdMT;
-        __syncthreads();  // previous tile's readers of X4/I4/T4 and red are done
+        __syncthreads();  // previous tile's readers of Xk/Ik/Nk and red are done
         float xval;
         {
             const int t = threadIdx.x >> 2, kk = threadIdx.x & 3;
@@ -531,24 +650,24 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
             const bool valid = m < p.M && k < p.K;
             xval = valid ? __ldg(p.x + (int64_t)m * p.K + k) : 0.0f;
             const float d = __fadd_rn(1.0f, __fdiv_rn(xval, p.vsat));
-            reinterpret_cast<float*>(X4)[threadIdx.x] = xval;
-            reinterpret_cast<float*>(I4)[threadIdx.x] = valid ? __fdiv_rn(1.0f, d) : 0.0f;
-            reinterpret_cast<float*>(T4)[threadIdx.x] =
-                valid ? __fdiv_rn(1.0f, __fmul_rn(__fmul_rn(p.vsat, d), d)) : 0.0f;
+            Xk[kk * kBwdMT + t] = xval;
+            Ik[kk * kBwdMT + t] = valid ? __fdiv_rn(1.0f, d) : 0.0f;
+            Nk[kk * kBwdMT + t] = valid ? -__fdiv_rn(1.0f, __fmul_rn(__fmul_rn(p.vsat, d), d)) : 0.0f;
         }
         float4 xr;
         bool xnan;
         block_range4(make_float4(xval, xval, INFINITY, -INFINITY), xval != xval, red, red_nan, xr, xnan);
         const bool fast = tile_in_table(xr.x, xr.y, wr.z, wr.w, xnan || wnan, p.dmin, p.scale, T);
 
-        float dx[kBwdTok * kBwdKT];
+        f32x2 dx2[4][kBwdKT];  // [token pair][input]
 #pragma unroll
-        for (int i = 0; i < kBwdTok * kBwdKT; ++i) dx[i] = 0.0f;
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int kk = 0; kk < kBwdKT; ++kk) dx2[i][kk] = pk2(0.0f, 0.0f);
 
-        // Register prefetch of chunk operands: g for the 8 tokens, thresholds
-        // of (o, k0..k0+3).
-        float gn[kBwdTok], wpn[kBwdKT], wnn[kBwdKT];
-        auto load_chunk = [&](int c) {
+        // Register prefetch of g (8 tokens of this warp, output of this lane).
+        float gn[kBwdTok];
+        auto load_g = [&](int c) {
             const int o = c * 32 + lane;
             const bool oin = o < p.O;
 #pragma unroll
@@ -556,36 +675,34 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
                 const int m = m0 + warp * kBwdTok + i;
                 gn[i] = (oin && m < p.M) ? __ldg(p.g + (int64_t)m * p.O + o) : 0.0f;
             }
-#pragma unroll
-            for (int kk = 0; kk < kBwdKT; ++kk) {
-                const bool valid = oin && k0 + kk < p.K;
-                wpn[kk] = valid ? __ldg(p.wp + (int64_t)o * p.K + k0 + kk) : 0.0f;
-                wnn[kk] = valid ? __ldg(p.wn + (int64_t)o * p.K + k0 + kk) : 0.0f;
-            }
         };
-        if (nchunks > 0) load_chunk(0);
+        if (nchunks > 0) load_g(0);
         for (int c = 0; c < nchunks; ++c) {
-            float g[kBwdTok], wp[kBwdKT], wn[kBwdKT];
+            float g[kBwdTok];
 #pragma unroll
             for (int i = 0; i < kBwdTok; ++i) g[i] = gn[i];
+            if (c + 1 < nchunks) load_g(c + 1);
+            // next chunk's thresholds (wrapping to chunk 0 for the next tile)
+            const float wnext = fetch_w(c + 1 < nchunks ? c + 1 : 0);
+            const float* ws = wsm + buf * (32 * 8);
+            f32x2 ap2[kBwdKT], an2[kBwdKT];
 #pragma unroll
-            for (int kk = 0; kk < kBwdKT; ++kk) {
-                wp[kk] = wpn[kk];
-                wn[kk] = wnn[kk];
-            }
-            if (c + 1 < nchunks) load_chunk(c + 1);
-            float ap[kBwdKT] = {0.f, 0.f, 0.f, 0.f}, an[kBwdKT] = {0.f, 0.f, 0.f, 0.f};
+            for (int kk = 0; kk < kBwdKT; ++kk) ap2[kk] = an2[kk] = pk2(0.0f, 0.0f);
             if (fast) {
-                bwd_chunk<false>(X4, I4, T4, g, wp, wn, tab_base, p.dmin, p.scale, fmax_, dx, ap, an);
+                bwd_chunk<false, kStride>(Xk, Ik, Nk, ws, g, lc, dx2, ap2, an2);
             } else {
-                bwd_chunk<true>(X4, I4, T4, g, wp, wn, tab_base, p.dmin, p.scale, fmax_, dx, ap, an);
+                bwd_chunk<true, kStride>(Xk, Ik, Nk, ws, g, lc, dx2, ap2, an2);
             }
+            wsm[(buf ^ 1) * (32 * 8) + threadIdx.x] = wnext;
             // Cross-warp sum of the dVth partials, accumulated into dWs.
-            float* xb = xch + xbuf * (8 * 8 * 32);
+            float* xb = xch + buf * (8 * 8 * 32);
 #pragma unroll
             for (int kk = 0; kk < kBwdKT; ++kk) {
-                xb[(warp * 8 + kk) * 32 + lane] = ap[kk];
-                xb[(warp * 8 + 4 + kk) * 32 + lane] = an[kk];
+                float a0, a1, b0, b1;
+                unpk2(ap2[kk], a0, a1);
+                unpk2(an2[kk], b0, b1);
+                xb[(warp * 8 + kk) * 32 + lane] = a0 + a1;
+                xb[(warp * 8 + 4 + kk) * 32 + lane] = b0 + b1;
             }
             __syncthreads();
             {
@@ -596,8 +713,14 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
                 const int o = c * 32 + lane;
                 dWs[((v >> 2) * opad + o) * kBwdKT + (v & 3)] += s;
             }
-            xbuf ^= 1;
+            buf ^= 1;
         }
+        float dx[kBwdTok * kBwdKT];  // element (token i, input kk) at i * 4 + kk
+#pragma unroll
+        for (int ip = 0; ip < 4; ++ip)
+#pragma unroll
+            for (int kk = 0; kk < kBwdKT; ++kk)
+                unpk2(dx2[ip][kk], dx[(2 * ip) * kBwdKT + kk], dx[(2 * ip + 1) * kBwdKT + kk]);
         // 32-lane transpose-reduce of dx: afterwards lane l holds the full sum
         // of element l = (token l/4, input l%4).
 #pragma unroll
@@ -713,7 +836,7 @@ const char* cimekv_last_error(void) { return g_last_error; }
 
 size_t cimekv_lut_bytes(int table_size) {
     if (table_size < 2 || table_size > CIMEKV_MAX_LUT_SIZE) return 0;
-    return fwd_table_bytes(table_size) + bwd_table_bytes(table_size);
+    return 2 * fwd_table_bytes(table_size);
 }
 
 int cimekv_lut_pack(const uint16_t* table_i, const uint16_t* table_ddelta, int table_size, void* lut,
@@ -723,11 +846,11 @@ int cimekv_lut_pack(const uint16_t* table_i, const uint16_t* table_ddelta, int t
     if (rc) return rc;
     if (!table_i || !table_ddelta || !lut) return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
     if (!aligned16(lut)) return set_error(CIMEKV_EINVAL_SHAPE, "lut must be 16-byte aligned");
-    const int fwd_words = (int)(fwd_table_bytes(table_size) / 4);
-    uint32_t* fwd = static_cast<uint32_t*>(lut);
-    uint2* bwd = reinterpret_cast<uint2*>(static_cast<unsigned char*>(lut) + fwd_table_bytes(table_size));
-    lut_pack_kernel<<<(fwd_words + 255) / 256, 256, 0, (cudaStream_t)stream>>>(table_i, table_ddelta, table_size,
-                                                                                fwd, bwd, fwd_words);
+    const int words = (int)(fwd_table_bytes(table_size) / 4);
+    uint32_t* lut_i = static_cast<uint32_t*>(lut);
+    uint32_t* lut_d = lut_i + words;
+    lut_pack_kernel<<<(words + 255) / 256, 256, 0, (cudaStream_t)stream>>>(table_i, table_ddelta, table_size,
+                                                                            lut_i, lut_d, words);
     return check_launch("lut_pack_kernel");
 }
 
@@ -818,13 +941,19 @@ int cimekv_backward(const float* x, const float* wpos, const float* wneg, const 
     int dev, sms, optin;
     if ((rc = current_device(&dev))) return rc;
     if ((rc = device_limits(dev, &sms, &optin))) return rc;
-    if ((rc = allow_smem(dev, 1, bwd_kernel, optin))) return rc;
+    const int stride = bwd_stride(table_size);
+    const int slot = stride == 4096 ? 1 : (stride == 8192 ? 2 : 3);
+    if (stride == 4096) rc = allow_smem(dev, slot, bwd_kernel<4096>, optin);
+    else if (stride == 8192) rc = allow_smem(dev, slot, bwd_kernel<8192>, optin);
+    else rc = allow_smem(dev, slot, bwd_kernel<16384>, optin);
+    if (rc) return rc;
     BwdParams p;
     p.x = x;
     p.wp = wpos;
     p.wn = wneg;
     p.g = grad_out;
-    p.lut = reinterpret_cast<const uint2*>(static_cast<const unsigned char*>(lut) + fwd_table_bytes(table_size));
+    p.lut_i = static_cast<const uint32_t*>(lut);
+    p.lut_d = p.lut_i + fwd_table_bytes(table_size) / 4;
     p.grad_x = grad_x;
     p.part = want_w ? static_cast<float*>(workspace) : nullptr;
     p.M = M;
@@ -837,7 +966,9 @@ int cimekv_backward(const float* x, const float* wpos, const float* wneg, const 
     p.scale = delta_scale;
     p.vsat = v_sat;
     dim3 grid(plan.kblocks, plan.nsplit);
-    bwd_kernel<<<grid, kBwdThreads, plan.smem, s>>>(p);
+    if (stride == 4096) bwd_kernel<4096><<<grid, kBwdThreads, plan.smem, s>>>(p);
+    else if (stride == 8192) bwd_kernel<8192><<<grid, kBwdThreads, plan.smem, s>>>(p);
+    else bwd_kernel<16384><<<grid, kBwdThreads, plan.smem, s>>>(p);
     if ((rc = check_launch("bwd_kernel"))) return rc;
     if (want_w) {
         const int64_t n = (int64_t)O * K;

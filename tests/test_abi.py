@@ -42,7 +42,7 @@ def test_binding_covers_header():
 
 def test_host_side_argument_checks(lib):
     assert lib.cimekv_abi_version() == 1
-    assert lib.cimekv_lut_bytes(4096) == 4096 * 12
+    assert lib.cimekv_lut_bytes(4096) == 4096 * 8
     assert lib.cimekv_lut_bytes(1) == 0
     assert lib.cimekv_lut_bytes(1 << 20) == 0
     rc = lib.cimekv_forward(None, None, None, None, -1, 4, 4, 4096, -9.0, 315.0, 8.26, -4.0, 4.0, None, None)
