@@ -103,6 +103,38 @@ int cimekv_lut_index(const float* delta, int n, int table_size,
                      float delta_min, float delta_scale,
                      int32_t* index, float* alpha, void* stream);
 
+/* Fixed device scratch of cimekv_backward_noalloc (32 MiB per GPU). */
+#define CIMEKV_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+
+/*
+ * Allocation-free variant of cimekv_backward; it has no counterpart in the
+ * reference.  Same arguments and results as cimekv_backward, minus the
+ * workspace: the token-split dVth partials go to a scratch array compiled into
+ * this library (CIMEKV_NOALLOC_SCRATCH_BYTES of static device memory, held by
+ * every GPU that loads the library until the process exits).  It is for callers
+ * that cannot call cudaMalloc or an allocator around this operator — e.g. code
+ * running under a memory pool it does not own, a host runtime with no device
+ * allocator bound, or a plugin that must not grow the process's footprint per
+ * call.  It allocates nothing and calls no allocating routine.
+ *   - The first call on a device looks up the scratch's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - Fails with CIMEKV_EWORKSPACE when 2*out_features*in_features*4 bytes
+ *     exceed the scratch (out*in > 4,194,304); larger token counts only lower
+ *     the number of token splits, never the result's correctness.
+ *   - All calls share the one scratch: calls that may run at the same time on
+ *     the GPU (different streams, different threads without ordering) race and
+ *     give wrong dVth.  Calls ordered on one stream are safe.  Each call
+ *     overwrites every scratch element it reads, so nothing needs clearing.
+ *   - Results are identical to cimekv_backward's up to the order of the
+ *     deterministic split reduction (which may use fewer splits).
+ */
+int cimekv_backward_noalloc(const float* x, const float* wpos, const float* wneg,
+                            const float* grad_out, const void* lut,
+                            int M, int K, int O, int table_size,
+                            float delta_min, float delta_scale, float v_sat,
+                            float* grad_x, float* grad_wpos, float* grad_wneg, void* stream);
+
 /*
  * Measurement utility with no counterpart in the reference: launches `blocks`
  * CTAs of 256 threads that each issue iters*128 independent FFMAs, and

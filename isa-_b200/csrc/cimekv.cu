@@ -994,3 +994,121 @@ int cimekv_lut_index(const float* delta, int n, int table_size, float delta_min,
 }
 
 }  // extern "C"
+
+// ----------------------------------------------- allocation-free backward --
+//
+// Scratch for callers that cannot allocate device memory themselves (see
+// cimekv_backward_noalloc in cimekv.h).  It lives in the library's own static
+// device memory: every GPU that loads the library holds these
+// CIMEKV_NOALLOC_SCRATCH_BYTES until the process exits.  Host code must not use
+// the symbol's name as a pointer; the device address is looked up once per
+// device with cudaGetSymbolAddress.
+
+static __device__ __align__(256) float g_noalloc_scratch[CIMEKV_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+namespace {
+
+std::mutex g_noalloc_mutex;
+float* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on device `dev` (which must be current).
+int noalloc_scratch(int dev, float** out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || ptr == nullptr) {
+            return set_error(CIMEKV_ECUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+        }
+        g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+    }
+    *out = g_noalloc_ptr[dev];
+    return CIMEKV_OK;
+}
+
+}  // namespace
+
+extern "C" int cimekv_backward_noalloc(const float* x, const float* wpos, const float* wneg,
+                                       const float* grad_out, const void* lut, int M, int K, int O,
+                                       int table_size, float delta_min, float delta_scale, float v_sat,
+                                       float* grad_x, float* grad_wpos, float* grad_wneg, void* stream) {
+    g_last_error[0] = '\0';
+    int rc = check_lut_size(table_size);
+    if (rc) return rc;
+    if (M < 0 || K < 0 || O < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative size M=%d K=%d O=%d", M, K, O);
+    if ((grad_wpos == nullptr) != (grad_wneg == nullptr))
+        return set_error(CIMEKV_EINVAL_SHAPE, "grad_wpos and grad_wneg must both be given or both be NULL");
+    const bool want_w = grad_wpos != nullptr;
+    // One token split needs 2*O*K floats of scratch; refuse what cannot fit.
+    const size_t per_split = (size_t)2 * (size_t)O * (size_t)K * sizeof(float);
+    if (want_w && per_split > CIMEKV_NOALLOC_SCRATCH_BYTES) {
+        return set_error(CIMEKV_EWORKSPACE,
+                         "cimekv_backward_noalloc: out_features*in_features = %lld needs %zu B of scratch per "
+                         "token split, above the library's fixed %zu B (at most %zu threshold pairs)",
+                         (long long)O * K, per_split, (size_t)CIMEKV_NOALLOC_SCRATCH_BYTES,
+                         (size_t)CIMEKV_NOALLOC_SCRATCH_BYTES / (2 * sizeof(float)));
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    if (K == 0) return CIMEKV_OK;
+    if (M == 0 || O == 0) {
+        if (want_w && O > 0) {
+            fill_zero_kernel<<<64, 256, 0, s>>>(grad_wpos, (int64_t)O * K);
+            fill_zero_kernel<<<64, 256, 0, s>>>(grad_wneg, (int64_t)O * K);
+        }
+        if (grad_x && M > 0) fill_zero_kernel<<<64, 256, 0, s>>>(grad_x, (int64_t)M * K);
+        return check_launch("fill_zero_kernel");
+    }
+    if (!grad_x && !want_w) return CIMEKV_OK;
+    if (!x || !wpos || !wneg || !grad_out || !lut) return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
+    if (!aligned16(lut)) return set_error(CIMEKV_EINVAL_SHAPE, "lut must be 16-byte aligned");
+    if (!(delta_scale > 0.0f)) return set_error(CIMEKV_EINVAL_SHAPE, "delta_scale must be > 0");
+    BwdPlan plan;
+    if ((rc = plan_backward(M, K, O, table_size, &plan))) return rc;
+    // Fewer token splits when the planned ones do not fit the fixed scratch.
+    const int max_split = (int)(CIMEKV_NOALLOC_SCRATCH_BYTES / per_split);
+    if (plan.nsplit > max_split) plan.nsplit = max_split;
+    int dev, sms, optin;
+    if ((rc = current_device(&dev))) return rc;
+    if ((rc = device_limits(dev, &sms, &optin))) return rc;
+    float* scratch = nullptr;
+    if (want_w && (rc = noalloc_scratch(dev, &scratch))) return rc;
+    const int stride = bwd_stride(table_size);
+    const int slot = stride == 4096 ? 1 : (stride == 8192 ? 2 : 3);
+    if (stride == 4096) rc = allow_smem(dev, slot, bwd_kernel<4096>, optin);
+    else if (stride == 8192) rc = allow_smem(dev, slot, bwd_kernel<8192>, optin);
+    else rc = allow_smem(dev, slot, bwd_kernel<16384>, optin);
+    if (rc) return rc;
+    BwdParams p;
+    p.x = x;
+    p.wp = wpos;
+    p.wn = wneg;
+    p.g = grad_out;
+    p.lut_i = static_cast<const uint32_t*>(lut);
+    p.lut_d = p.lut_i + fwd_table_bytes(table_size) / 4;
+    p.grad_x = grad_x;
+    // Every split slice of the scratch is fully overwritten by the kernel before
+    // the reduction reads it, so nothing left from an earlier call is used.
+    p.part = want_w ? scratch : nullptr;
+    p.M = M;
+    p.K = K;
+    p.O = O;
+    p.T = table_size;
+    p.tiles_m = plan.tiles_m;
+    p.nsplit = plan.nsplit;
+    p.dmin = delta_min;
+    p.scale = delta_scale;
+    p.vsat = v_sat;
+    dim3 grid(plan.kblocks, plan.nsplit);
+    if (stride == 4096) bwd_kernel<4096><<<grid, kBwdThreads, plan.smem, s>>>(p);
+    else if (stride == 8192) bwd_kernel<8192><<<grid, kBwdThreads, plan.smem, s>>>(p);
+    else bwd_kernel<16384><<<grid, kBwdThreads, plan.smem, s>>>(p);
+    if ((rc = check_launch("bwd_kernel"))) return rc;
+    if (want_w) {
+        const int64_t n = (int64_t)O * K;
+        int blocks = (int)((n + 255) / 256);
+        if (blocks > sms * 8) blocks = sms * 8;
+        bwd_reduce_kernel<<<blocks, 256, 0, s>>>(p.part, plan.nsplit, n, grad_wpos, grad_wneg);
+        if ((rc = check_launch("bwd_reduce_kernel"))) return rc;
+    }
+    return CIMEKV_OK;
+}

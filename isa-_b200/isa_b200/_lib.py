@@ -31,6 +31,8 @@ SIGNATURES = {
     "cimekv_backward_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, _c_int]),
     "cimekv_backward": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
                                  _c_float, _c_float, _c_float, _vp, _vp, _vp, _vp, _c_size, _vp]),
+    "cimekv_backward_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+                                         _c_float, _c_float, _c_float, _vp, _vp, _vp, _vp]),
     "cimekv_lut_index": (_c_int, [_vp, _c_int, _c_int, _c_float, _c_float, _vp, _vp, _vp]),
     "cimekv_fp32_probe": (_c_int, [_vp, _c_int, _c_int, ctypes.POINTER(ctypes.c_longlong), _vp]),
 }
@@ -126,6 +128,17 @@ def backward(x, wpos, wneg, grad_out, lut, table_size, delta_min, delta_scale, v
                                 _ptr(grad_x), _ptr(grad_wpos), _ptr(grad_wneg),
                                 _ptr(workspace), ws_bytes, _stream(stream))
     _check(rc, "cimekv_backward")
+
+
+def backward_noalloc(x, wpos, wneg, grad_out, lut, table_size, delta_min, delta_scale, v_sat,
+                     grad_x, grad_wpos, grad_wneg, stream=None) -> None:
+    """cimekv_backward without a workspace: uses the library's fixed scratch."""
+    m, k = x.shape
+    o = wpos.shape[0]
+    rc = load().cimekv_backward_noalloc(_ptr(x), _ptr(wpos), _ptr(wneg), _ptr(grad_out), _ptr(lut), m, k, o,
+                                        int(table_size), delta_min, delta_scale, v_sat,
+                                        _ptr(grad_x), _ptr(grad_wpos), _ptr(grad_wneg), _stream(stream))
+    _check(rc, "cimekv_backward_noalloc")
 
 
 def lut_index(delta: torch.Tensor, table_size: int, delta_min: float, delta_scale: float,
