@@ -49,7 +49,9 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference_gpu"], default="ours",
+                    help="reference_gpu: informational run of the unmodified reference's own GPU path "
+                         "(Triton forward + JIT CUDA backward) installed in baseline/_ref")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gpt_m_ffn")
     ap.add_argument("--cpu-sample-tokens", type=int, default=1024,
                     help="tokens of the CPU baseline sample (our arm)")
@@ -159,11 +161,22 @@ def fp32_peak(dev) -> dict:
     return {"burst": ops / (best * 1e-3), "sustained": n * ops / (s.elapsed_time(e) * 1e-3)}
 
 
-def make_ffn(wl, dev, seed=0):
+def make_ffn(wl, dev, seed=0, reference=False):
     import torch
 
-    from isa_b200 import make_flash_transistor_ekv_config
-    from isa_b200.operators.cim import PhysicalFFN
+    if reference:
+        # The unmodified reference package (pip-installed into baseline/_ref),
+        # through its own public module API: Triton LUT forward, JIT-built CUDA
+        # shared-memory backward (its defaults).
+        ref_dir = ROOT / "baseline" / "_ref"
+        if not (ref_dir / "isa").exists():
+            raise SystemExit("baseline/_ref is not installed")
+        sys.path.insert(0, str(ref_dir))
+        from isa.device_models.config import make_flash_transistor_ekv_config
+        from isa.operators.cim import PhysicalFFN
+    else:
+        from isa_b200 import make_flash_transistor_ekv_config
+        from isa_b200.operators.cim import PhysicalFFN
 
     cfg = make_flash_transistor_ekv_config(default_lut_size=wl["lut"])
     cfg["LUT_DELTA_SIZE"] = wl["lut"]
@@ -285,7 +298,8 @@ def run_ours(args, wl):
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    ffn, cfg = make_ffn(wl, dev)
+    refgpu = args.impl == "reference_gpu"
+    ffn, cfg = make_ffn(wl, dev, reference=refgpu)
     B, S, d = wl["batch"], wl["seq"], wl["d"]
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     x = torch.randn(B, S, d, device=dev, generator=gen)  # post-LayerNorm scale
@@ -337,10 +351,10 @@ def run_ours(args, wl):
         dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
     e2e_value = world * cells_step * args.steps / (float(e_ms.item()) * 1e-3)
 
-    kern = time_kernels(ffn, cfg, x, dev) if rank == 0 else None
+    kern = time_kernels(ffn, cfg, x, dev) if rank == 0 and not refgpu else None
     peak = fp32_peak(dev) if rank == 0 else None
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not refgpu:
         from oracle import oracle
         c, sec = cpu_sample(wl, args.cpu_sample_tokens)
         cpu = {"value": c / sec / 1e9, "unit": "Gcell-evals/s", "cores": oracle.max_threads(), "kind": "port",
@@ -348,7 +362,20 @@ def run_ours(args, wl):
                          f"oracle/cimekv_oracle.c with OpenMP, {sec:.1f} s"}
     if world > 1:
         dist.barrier()
-    if rank == 0:
+    if rank == 0 and refgpu:
+        rec = {"metric": "CIM-FFN fwd+bwd Gcell-evals/s", "value": value / 1e9, "unit": "Gcell-evals/s",
+               "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_total / args.steps,
+               "higher_is_better": True, "scaling": "weak", "dtype": "f32", "impl": "reference_gpu",
+               "config": {"workload": args.workload, "model": wl["model"], "tokens_per_gpu": tokens,
+                          "lut_size": wl["lut"], "parallelism": f"dp{world}"},
+               "tokens_per_s": world * tokens * args.steps / (ms_total * 1e-3),
+               "step_frac_of_fp32_peak": value * (OPS_FWD + OPS_BWD) / peak["sustained"],
+               "e2e": {"value": e2e_value / 1e9, "unit": "Gcell-evals/s"},
+               "clocks": clocks.summary(),
+               "note": "unmodified reference package from baseline/_ref: Triton _forward_kernel + JIT-built "
+                       "ekv_grad_x_shared/ekv_grad_w_shared CUDA kernels, same workload and timing"}
+        print(json.dumps(rec), flush=True)
+    elif rank == 0:
         clk = clocks.summary()
         # Dominant kernel: the one with the largest total time per step.
         per = []
