@@ -32,6 +32,14 @@
 
 #include "cimekv.h"
 
+// Compile-time tuning knobs.
+#ifndef CIMEKV_FWD_MIN_BLOCKS
+#define CIMEKV_FWD_MIN_BLOCKS 3  // resident forward CTAs per SM the register budget is sized for
+#endif
+#ifndef CIMEKV_FWD_KK_UNROLL
+#define CIMEKV_FWD_KK_UNROLL 2
+#endif
+
 namespace {
 
 // ---------------------------------------------------------------- errors --
@@ -303,6 +311,7 @@ __global__ void lut_index_kernel(const float* __restrict__ delta, int n, int T, 
 // Persistent grid: each CTA stages the table once and walks a strided list of
 // tiles.
 
+constexpr int kFwdKkUnroll = CIMEKV_FWD_KK_UNROLL;
 constexpr int kFwdThreads = 256;
 constexpr int kFwdMT = 64;
 constexpr int kFwdOT = 64;
@@ -326,7 +335,7 @@ __device__ __forceinline__ void fwd_chunk(const float* __restrict__ xs, const fl
                                           const float* __restrict__ ps, const float* __restrict__ ns,
                                           const LutConsts& c, f32x2 (&acc)[4][2]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll 2
+#pragma unroll kFwdKkUnroll
     for (int kk = 0; kk < kFwdKC; ++kk) {
         const float4 xa = *reinterpret_cast<const float4*>(xs + kk * kFwdLD + warp * 8);
         const float4 xb = *reinterpret_cast<const float4*>(xs + kk * kFwdLD + warp * 8 + 4);
@@ -353,7 +362,7 @@ __device__ __forceinline__ void fwd_chunk(const float* __restrict__ xs, const fl
     }
 }
 
-__global__ void __launch_bounds__(kFwdThreads, 2) fwd_kernel(FwdParams p) {
+__global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel(FwdParams p) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int T = p.T;
     uint32_t* tab = reinterpret_cast<uint32_t*>(smem);
@@ -889,7 +898,7 @@ int cimekv_forward(const float* x, const float* wpos, const float* wneg, const v
     p.out_max = out_max;
     const long ntiles = (long)((M + kFwdMT - 1) / kFwdMT) * ((O + kFwdOT - 1) / kFwdOT);
     int resident = (int)((228 * 1024) / (smem + 1024));
-    if (resident > 2) resident = 2;
+    if (resident > CIMEKV_FWD_MIN_BLOCKS) resident = CIMEKV_FWD_MIN_BLOCKS;
     if (resident < 1) resident = 1;
     long grid = (long)sms * resident;
     if (grid > ntiles) grid = ntiles;
