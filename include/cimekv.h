@@ -69,6 +69,36 @@ int cimekv_forward(const float* x, const float* wpos, const float* wneg,
                    float out_min, float out_max, float* out, void* stream);
 
 /*
+ * Forward with the TIA stage fused into the epilogue: besides
+ * idiff = clamp(I_diff, idiff_min, idiff_max) (as cimekv_forward, may be NULL
+ * when not needed) it writes out = clamp(idiff * (*r_tia), out_min, out_max),
+ * the reference's `idiff * r_tia` then `clamp` done by torch in
+ * CIMLinear.forward (src/isa/operators/cim.py:192-193).  r_tia is a DEVICE
+ * pointer to one float, so a learnable gain needs no host synchronisation.
+ */
+int cimekv_forward_tia(const float* x, const float* wpos, const float* wneg,
+                       const void* lut, int M, int K, int O, int table_size,
+                       float delta_min, float delta_scale, float v_sat,
+                       float idiff_min, float idiff_max, const float* r_tia,
+                       float out_min, float out_max, float* idiff, float* out,
+                       void* stream);
+
+/* Workspace bytes of cimekv_tia_backward (a fixed, small number). */
+size_t cimekv_tia_workspace_bytes(long long n);
+
+/*
+ * Backward of the TIA stage, one pass over n = M*O elements: with
+ * v = idiff * r_tia, grad_idiff = [out_min <= v <= out_max] * grad_out * r_tia
+ * and *grad_r_tia = sum [..] * grad_out * idiff (device scalar, deterministic
+ * order).  Replaces the autograd of `idiff * r_tia` and `clamp` in the
+ * reference's CIMLinear.forward (cim.py:192-193).
+ */
+int cimekv_tia_backward(const float* grad_out, const float* idiff, const float* r_tia,
+                        long long n, float out_min, float out_max,
+                        float* grad_idiff, float* grad_r_tia,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Workspace bytes cimekv_backward needs for these sizes on the current device.
  */
 size_t cimekv_backward_workspace_bytes(int M, int K, int O, int table_size);

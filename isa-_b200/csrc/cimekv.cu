@@ -325,10 +325,17 @@ struct FwdParams {
     const float* wp;
     const float* wn;
     const uint32_t* lut;
-    float* out;
+    float* out;               // I_diff, clamped to [out_min, out_max]
+    const float* r_tia;       // device scalar R_TIA (used when tia_out != nullptr)
+    float* tia_out;           // optional clamp(I_diff * R_TIA, tia_lo, tia_hi)
     int M, K, O, T;
-    float dmin, scale, vsat, out_min, out_max;
+    float dmin, scale, vsat, out_min, out_max, tia_lo, tia_hi;
 };
+
+// torch.clamp semantics (NaN passes through).
+__device__ __forceinline__ float clamp_keep_nan(float v, float lo, float hi) {
+    return v < lo ? lo : (v > hi ? hi : v);
+}
 
 template <bool kClamp>
 __device__ __forceinline__ void fwd_chunk(const float* __restrict__ xs, const float* __restrict__ is,
@@ -387,6 +394,7 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
     lc.dmin2 = pk2(p.dmin, p.dmin);
     lc.scale2 = pk2(p.scale, p.scale);
     lc.two23 = pk2(kTwo23, kTwo23);
+    const float r_tia = p.tia_out != nullptr ? __ldg(p.r_tia) : 0.0f;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_m = (p.M + kFwdMT - 1) / kFwdMT;
     const int tiles_o = (p.O + kFwdOT - 1) / kFwdOT;
@@ -457,7 +465,10 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
                 float v0, v1;
                 unpk2(acc[i >> 1][j], v0, v1);
                 if (o < p.O) {
-                    p.out[(int64_t)m * p.O + o] = fminf(fmaxf((i & 1) ? v1 : v0, p.out_min), p.out_max);
+                    const float id = fminf(fmaxf((i & 1) ? v1 : v0, p.out_min), p.out_max);
+                    p.out[(int64_t)m * p.O + o] = id;
+                    if (p.tia_out != nullptr)  // fused TIA: the reference's `I_diff * r_tia` then clamp
+                        p.tia_out[(int64_t)m * p.O + o] = clamp_keep_nan(__fmul_rn(id, r_tia), p.tia_lo, p.tia_hi);
                 }
             }
         }
@@ -779,6 +790,53 @@ __global__ void fill_zero_kernel(float* __restrict__ p, int64_t n) {
         p[i] = 0.0f;
 }
 
+// ---------------------------------------------------------- TIA stage --
+//
+// Backward of out = clamp(I_diff * R_TIA, lo, hi) (reference cim.py:192-193,
+// differentiated by autograd there): grad_I_diff = [lo <= I_diff*R <= hi] * g * R
+// and dL/dR = sum [..] * g * I_diff.  One pass over [M,O]; the sum goes through
+// fixed per-block partials and a one-block reduction (deterministic).
+
+constexpr int kTiaBlocks = 592;
+
+__global__ void __launch_bounds__(256) tia_bwd_kernel(const float* __restrict__ g, const float* __restrict__ idiff,
+                                                      const float* __restrict__ r_ptr, int64_t n, float lo, float hi,
+                                                      float* __restrict__ g_idiff, float* __restrict__ partial) {
+    const float r = __ldg(r_ptr);
+    float acc = 0.0f;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float id = idiff[i], gv = g[i];
+        const float v = __fmul_rn(id, r);
+        const bool pass = (v >= lo) && (v <= hi);
+        const float gm = pass ? gv : 0.0f;
+        g_idiff[i] = __fmul_rn(gm, r);
+        acc = fmaf(gm, id, acc);
+    }
+    __shared__ float red[8];
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+        partial[blockIdx.x] = t;
+    }
+}
+
+__global__ void sum_partials_kernel(const float* __restrict__ partial, int n, float* __restrict__ out) {
+    __shared__ float red[256];
+    float t = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) t += partial[i];
+    red[threadIdx.x] = t;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float u = 0.0f;
+        for (int i = 0; i < (int)blockDim.x; ++i) u += red[i];
+        out[0] = u;
+    }
+}
+
 // Token splits of the backward: enough CTAs to fill the GPU in whole waves.
 struct BwdPlan {
     int kblocks, tiles_m, nsplit;
@@ -863,15 +921,16 @@ int cimekv_lut_pack(const uint16_t* table_i, const uint16_t* table_ddelta, int t
     return check_launch("lut_pack_kernel");
 }
 
-int cimekv_forward(const float* x, const float* wpos, const float* wneg, const void* lut, int M, int K, int O,
-                   int table_size, float delta_min, float delta_scale, float v_sat, float out_min, float out_max,
-                   float* out, void* stream) {
+static int launch_forward(const float* x, const float* wpos, const float* wneg, const void* lut, int M, int K,
+                          int O, int table_size, float delta_min, float delta_scale, float v_sat, float out_min,
+                          float out_max, float* out, const float* r_tia, float tia_lo, float tia_hi, float* tia_out,
+                          void* stream) {
     g_last_error[0] = '\0';
     int rc = check_lut_size(table_size);
     if (rc) return rc;
     if (M < 0 || K < 0 || O < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative size M=%d K=%d O=%d", M, K, O);
     if (M == 0 || O == 0) return CIMEKV_OK;
-    if (!lut || !out || (K > 0 && (!x || !wpos || !wneg)))
+    if (!lut || !out || (K > 0 && (!x || !wpos || !wneg)) || (tia_out && !r_tia))
         return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
     if (!aligned16(lut)) return set_error(CIMEKV_EINVAL_SHAPE, "lut must be 16-byte aligned");
     if (!(delta_scale > 0.0f)) return set_error(CIMEKV_EINVAL_SHAPE, "delta_scale must be > 0");
@@ -896,6 +955,10 @@ int cimekv_forward(const float* x, const float* wpos, const float* wneg, const v
     p.vsat = v_sat;
     p.out_min = out_min;
     p.out_max = out_max;
+    p.r_tia = r_tia;
+    p.tia_out = tia_out;
+    p.tia_lo = tia_lo;
+    p.tia_hi = tia_hi;
     const long ntiles = (long)((M + kFwdMT - 1) / kFwdMT) * ((O + kFwdOT - 1) / kFwdOT);
     int resident = (int)((228 * 1024) / (smem + 1024));
     if (resident > CIMEKV_FWD_MIN_BLOCKS) resident = CIMEKV_FWD_MIN_BLOCKS;
@@ -904,6 +967,49 @@ int cimekv_forward(const float* x, const float* wpos, const float* wneg, const v
     if (grid > ntiles) grid = ntiles;
     fwd_kernel<<<(unsigned)grid, kFwdThreads, smem, (cudaStream_t)stream>>>(p);
     return check_launch("fwd_kernel");
+}
+
+int cimekv_forward(const float* x, const float* wpos, const float* wneg, const void* lut, int M, int K, int O,
+                   int table_size, float delta_min, float delta_scale, float v_sat, float out_min, float out_max,
+                   float* out, void* stream) {
+    return launch_forward(x, wpos, wneg, lut, M, K, O, table_size, delta_min, delta_scale, v_sat, out_min, out_max,
+                          out, nullptr, 0.0f, 0.0f, nullptr, stream);
+}
+
+int cimekv_forward_tia(const float* x, const float* wpos, const float* wneg, const void* lut, int M, int K, int O,
+                       int table_size, float delta_min, float delta_scale, float v_sat, float idiff_min,
+                       float idiff_max, const float* r_tia, float out_min, float out_max, float* idiff, float* out,
+                       void* stream) {
+    if (!out || !r_tia) {
+        g_last_error[0] = '\0';
+        return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
+    }
+    return launch_forward(x, wpos, wneg, lut, M, K, O, table_size, delta_min, delta_scale, v_sat, idiff_min,
+                          idiff_max, idiff, r_tia, out_min, out_max, out, stream);
+}
+
+size_t cimekv_tia_workspace_bytes(long long n) {
+    (void)n;
+    return (size_t)kTiaBlocks * sizeof(float);
+}
+
+int cimekv_tia_backward(const float* grad_out, const float* idiff, const float* r_tia, long long n, float out_min,
+                        float out_max, float* grad_idiff, float* grad_r_tia, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+    g_last_error[0] = '\0';
+    if (n < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative n");
+    if (!r_tia || !grad_r_tia || (n > 0 && (!grad_out || !idiff || !grad_idiff)))
+        return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
+    if (!workspace || workspace_bytes < (size_t)kTiaBlocks * sizeof(float))
+        return set_error(CIMEKV_EWORKSPACE, "TIA backward workspace needs %zu B", (size_t)kTiaBlocks * sizeof(float));
+    cudaStream_t s = (cudaStream_t)stream;
+    float* partial = static_cast<float*>(workspace);
+    tia_bwd_kernel<<<kTiaBlocks, 256, 0, s>>>(grad_out, idiff, r_tia, (int64_t)n, out_min, out_max, grad_idiff,
+                                              partial);
+    int rc = check_launch("tia_bwd_kernel");
+    if (rc) return rc;
+    sum_partials_kernel<<<1, 256, 0, s>>>(partial, kTiaBlocks, grad_r_tia);
+    return check_launch("sum_partials_kernel");
 }
 
 size_t cimekv_backward_workspace_bytes(int M, int K, int O, int table_size) {

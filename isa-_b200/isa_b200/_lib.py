@@ -28,6 +28,12 @@ SIGNATURES = {
     "cimekv_lut_pack": (_c_int, [_vp, _vp, _c_int, _vp, _vp]),
     "cimekv_forward": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
                                 _c_float, _c_float, _c_float, _c_float, _c_float, _vp, _vp]),
+    "cimekv_forward_tia": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+                                    _c_float, _c_float, _c_float, _c_float, _c_float, _vp,
+                                    _c_float, _c_float, _vp, _vp, _vp]),
+    "cimekv_tia_workspace_bytes": (_c_size, [ctypes.c_longlong]),
+    "cimekv_tia_backward": (_c_int, [_vp, _vp, _vp, ctypes.c_longlong, _c_float, _c_float, _vp, _vp, _vp,
+                                     _c_size, _vp]),
     "cimekv_backward_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, _c_int]),
     "cimekv_backward": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
                                  _c_float, _c_float, _c_float, _vp, _vp, _vp, _vp, _c_size, _vp]),
@@ -112,6 +118,24 @@ def forward(x, wpos, wneg, lut, table_size, delta_min, delta_scale, v_sat, out_m
     rc = load().cimekv_forward(_ptr(x), _ptr(wpos), _ptr(wneg), _ptr(lut), m, k, o, int(table_size),
                                delta_min, delta_scale, v_sat, out_min, out_max, _ptr(out), _stream(stream))
     _check(rc, "cimekv_forward")
+
+
+def forward_tia(x, wpos, wneg, lut, table_size, delta_min, delta_scale, v_sat, idiff_min, idiff_max, r_tia,
+                out_min, out_max, idiff, out, stream=None) -> None:
+    m, k = x.shape
+    o = wpos.shape[0]
+    rc = load().cimekv_forward_tia(_ptr(x), _ptr(wpos), _ptr(wneg), _ptr(lut), m, k, o, int(table_size),
+                                   delta_min, delta_scale, v_sat, idiff_min, idiff_max, _ptr(r_tia),
+                                   out_min, out_max, _ptr(idiff), _ptr(out), _stream(stream))
+    _check(rc, "cimekv_forward_tia")
+
+
+def tia_backward(grad_out, idiff, r_tia, out_min, out_max, grad_idiff, grad_r_tia, stream=None) -> None:
+    n = idiff.numel()
+    ws = torch.empty(int(load().cimekv_tia_workspace_bytes(n)), dtype=torch.uint8, device=idiff.device)
+    rc = load().cimekv_tia_backward(_ptr(grad_out), _ptr(idiff), _ptr(r_tia), n, out_min, out_max,
+                                    _ptr(grad_idiff), _ptr(grad_r_tia), _ptr(ws), ws.numel(), _stream(stream))
+    _check(rc, "cimekv_tia_backward")
 
 
 def backward_workspace_bytes(m: int, k: int, o: int, table_size: int) -> int:

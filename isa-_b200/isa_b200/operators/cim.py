@@ -21,7 +21,7 @@ import torch
 import torch.nn as nn
 
 from isa_b200.device_models.config import FLASH_TRANSISTOR_EKV_CONFIG as PHYSICAL_CONFIG
-from isa_b200.kernels.transformer_ffn.ekv_lut import cuda_lut_ekv_matmul
+from isa_b200.kernels.transformer_ffn.ekv_lut import cuda_lut_ekv_matmul, cuda_lut_ekv_matmul_tia
 
 
 class VoltageMapping(nn.Module):
@@ -160,11 +160,11 @@ class CIMLinear(nn.Module):
         if in_f != self.in_features:
             raise ValueError(f"expected {self.in_features} input features, got {in_f}")
         _lut_approx(self.cfg)
-        v_lo = float(self.cfg.get("V_signed_min", -4.0))
-        v_hi = float(self.cfg.get("V_signed_max", 4.0))
-        r_tia = self.r_tia.to(device=x.device, dtype=torch.float32).view(1, 1, 1)
-        idiff = cuda_lut_ekv_matmul(x.reshape(b * n, in_f), self.vth_pos, self.vth_neg, self.cfg)
-        out = (idiff.view(b, n, self.out_features) * r_tia).clamp(v_lo, v_hi)
+        # I_diff, * R_TIA and the signed clamp in one fused kernel (reference:
+        # LUT matmul, then `* r_tia` and `clamp` in torch).
+        r_tia = self.r_tia.to(device=x.device, dtype=torch.float32)
+        out = cuda_lut_ekv_matmul_tia(x.reshape(b * n, in_f), self.vth_pos, self.vth_neg, r_tia, self.cfg)
+        out = out.view(b, n, self.out_features)
         if self.track_output_stats:
             with torch.no_grad():
                 self._stat_total.add_(out.numel())
