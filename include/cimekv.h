@@ -124,6 +124,26 @@ int cimekv_backward(const float* x, const float* wpos, const float* wneg,
                     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Exact-formula path (cfg ekv_approx != "lut"): the same forward and fused
+ * backward with the EKV branch current evaluated per cell instead of looked up,
+ *   I(dV) = I_S (sp(u1)^2 - sp(u2)^2),  u1 = dV*inv_2nut, u2 = (dV - V_D)*inv_2nut,
+ *   sp(u) = u for u > 20, log(1 + e^u) otherwise,
+ * out[m,o] = sum_k (I(x-wpos) - I(x-wneg)) / (1 + x/v_sat), unclamped.
+ * Replaces the reference's exact Triton kernels _forward_kernel, _grad_x_kernel
+ * and _grad_w_kernel (src/isa/kernels/transformer_ffn/ekv_triton.py:69-150),
+ * reached through triton_ekv_matmul (ekv_triton.py:211-214, cim.py:186).
+ */
+int cimekv_exact_forward(const float* x, const float* wpos, const float* wneg,
+                         int M, int K, int O, float inv_2nut, float v_d, float i_s,
+                         float v_sat, float* out, void* stream);
+size_t cimekv_exact_backward_workspace_bytes(int M, int K, int O);
+int cimekv_exact_backward(const float* x, const float* wpos, const float* wneg,
+                          const float* grad_out, int M, int K, int O,
+                          float inv_2nut, float v_d, float i_s, float v_sat,
+                          float* grad_x, float* grad_wpos, float* grad_wneg,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Index selection of one lookup, for parity tests: for each dV in delta[n],
  * writes the table entry i0 the kernels use and the interpolation weight a,
  * computed by the same device code as the forward and backward

@@ -27,6 +27,7 @@
 
 #include <cstdarg>
 #include <cstdint>
+#include <cmath>
 #include <cstdio>
 #include <mutex>
 
@@ -68,7 +69,7 @@ constexpr int kMaxDevices = 64;
 std::mutex g_dev_mutex;
 int g_sm_count[kMaxDevices] = {0};
 int g_smem_optin[kMaxDevices] = {0};
-bool g_attr_set[kMaxDevices][4] = {};
+bool g_attr_set[kMaxDevices][8] = {};
 
 int current_device(int* dev) {
     cudaError_t e = cudaGetDevice(dev);
@@ -188,7 +189,47 @@ struct LutConsts {
     f32x2 dmin2, scale2, two23;
     float fmax_;
     uint32_t tab_base;
+    // exact-formula mode: 1/(2 n U_T), V_D, I_S, 2 I_S/(2 n U_T), exp(-V_D/(2 n U_T))
+    float inv, vd, i_s, di_s, kappa;
 };
+
+// ---- exact EKV branch current (no table) ----
+// I(dV)      = I_S (sp(u1)^2 - sp(u2)^2),  u1 = dV/(2nU_T), u2 = (dV - V_D)/(2nU_T)
+// dI/d(dV)   = I_S 2/(2nU_T) (sp(u1) sig(u1) - sp(u2) sig(u2))
+// with sp(u) = u for u > 20 else log(1 + e^u) (the reference's _softplus,
+// ekv_triton.py:23-25, and torch's softplus threshold), sig = e^u/(1+e^u).
+// e^u2 is taken as e^u1 * exp(-V_D/(2nU_T)).
+__device__ __forceinline__ void ekv_exact1(float dv, const LutConsts& c, float& base, float* deriv) {
+    const float u1 = __fmul_rn(dv, c.inv);
+    const float u2 = __fmul_rn(__fsub_rn(dv, c.vd), c.inv);
+    const float t1 = __expf(u1);
+    const float t2 = t1 * c.kappa;
+    const float sp1 = u1 > 20.0f ? u1 : log1pf(t1);  // accurate for small t (subthreshold)
+    const float sp2 = u2 > 20.0f ? u2 : log1pf(t2);
+    base = c.i_s * (sp1 * sp1 - sp2 * sp2);
+    if (deriv != nullptr) {
+        const float s1 = u1 > 20.0f ? 1.0f : t1 * __fdividef(1.0f, 1.0f + t1);
+        const float s2 = u2 > 20.0f ? 1.0f : t2 * __fdividef(1.0f, 1.0f + t2);
+        *deriv = c.di_s * (sp1 * s1 - sp2 * s2);
+    }
+}
+
+__device__ __forceinline__ f32x2 exact_fwd2(f32x2 xx, f32x2 ww, const LutConsts& c) {
+    float d0, d1, b0, b1;
+    unpk2(sub2(xx, ww), d0, d1);
+    ekv_exact1(d0, c, b0, nullptr);
+    ekv_exact1(d1, c, b1, nullptr);
+    return pk2(b0, b1);
+}
+
+__device__ __forceinline__ void exact_bwd2(f32x2 xx, f32x2 ww, const LutConsts& c, f32x2& base, f32x2& deriv) {
+    float d0, d1, b0, b1, g0, g1;
+    unpk2(sub2(xx, ww), d0, d1);
+    ekv_exact1(d0, c, b0, &g0);
+    ekv_exact1(d1, c, b1, &g1);
+    base = pk2(b0, b1);
+    deriv = pk2(g0, g1);
+}
 
 // Table coordinate of two lookups (two tokens against one threshold):
 // returns the bit patterns of t = f + 2^23 (rz) per half and a = f - trunc(f).
@@ -330,6 +371,7 @@ struct FwdParams {
     float* tia_out;           // optional clamp(I_diff * R_TIA, tia_lo, tia_hi)
     int M, K, O, T;
     float dmin, scale, vsat, out_min, out_max, tia_lo, tia_hi;
+    float inv, vd, i_s, di_s, kappa;  // exact-formula mode
 };
 
 // torch.clamp semantics (NaN passes through).
@@ -337,7 +379,7 @@ __device__ __forceinline__ float clamp_keep_nan(float v, float lo, float hi) {
     return v < lo ? lo : (v > hi ? hi : v);
 }
 
-template <bool kClamp>
+template <bool kClamp, bool kExact>
 __device__ __forceinline__ void fwd_chunk(const float* __restrict__ xs, const float* __restrict__ is,
                                           const float* __restrict__ ps, const float* __restrict__ ns,
                                           const LutConsts& c, f32x2 (&acc)[4][2]) {
@@ -361,14 +403,15 @@ __device__ __forceinline__ void fwd_chunk(const float* __restrict__ xs, const fl
         for (int ip = 0; ip < 4; ++ip) {
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const f32x2 vp = lut_fwd2<kClamp>(xx[ip], wp[j], c);
-                const f32x2 vn = lut_fwd2<kClamp>(xx[ip], wn[j], c);
+                const f32x2 vp = kExact ? exact_fwd2(xx[ip], wp[j], c) : lut_fwd2<kClamp>(xx[ip], wp[j], c);
+                const f32x2 vn = kExact ? exact_fwd2(xx[ip], wn[j], c) : lut_fwd2<kClamp>(xx[ip], wn[j], c);
                 acc[ip][j] = fma2(sub2(vp, vn), iv[ip], acc[ip][j]);
             }
         }
     }
 }
 
+template <bool kExact>
 __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel(FwdParams p) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int T = p.T;
@@ -394,6 +437,11 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
     lc.dmin2 = pk2(p.dmin, p.dmin);
     lc.scale2 = pk2(p.scale, p.scale);
     lc.two23 = pk2(kTwo23, kTwo23);
+    lc.inv = p.inv;
+    lc.vd = p.vd;
+    lc.i_s = p.i_s;
+    lc.di_s = p.di_s;
+    lc.kappa = p.kappa;
     const float r_tia = p.tia_out != nullptr ? __ldg(p.r_tia) : 0.0f;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_m = (p.M + kFwdMT - 1) / kFwdMT;
@@ -449,10 +497,12 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
             bool tnan;
             block_range4(rng, nan, red, red_nan, tr, tnan);  // includes the barrier
             if (c + 1 < nchunks) load_chunk((c + 1) * kFwdKC);
-            if (tile_in_table(tr.x, tr.y, tr.z, tr.w, tnan, p.dmin, p.scale, T)) {
-                fwd_chunk<false>(xs, is, ps, ns, lc, acc);
+            if (kExact) {
+                fwd_chunk<false, true>(xs, is, ps, ns, lc, acc);
+            } else if (tile_in_table(tr.x, tr.y, tr.z, tr.w, tnan, p.dmin, p.scale, T)) {
+                fwd_chunk<false, false>(xs, is, ps, ns, lc, acc);
             } else {
-                fwd_chunk<true>(xs, is, ps, ns, lc, acc);
+                fwd_chunk<true, false>(xs, is, ps, ns, lc, acc);
             }
         }
 #pragma unroll
@@ -515,14 +565,15 @@ struct BwdParams {
     int M, K, O, T;
     int tiles_m, nsplit;
     float dmin, scale, vsat;
+    float inv, vd, i_s, di_s, kappa;  // exact-formula mode (kStride == 0)
 };
 
 // Table stride (words) of the backward: the smallest supported size >= T.
 int bwd_stride(int T) { return T <= 4096 ? 4096 : (T <= 8192 ? 8192 : 16384); }
 
-size_t bwd_smem_bytes(int T, int O) {
+size_t bwd_smem_bytes_stride(int stride, int O) {
     const int opad = (O + 31) / 32 * 32;
-    return (size_t)8 * bwd_stride(T)                 // I and dI/dV pair tables
+    return (size_t)8 * stride                        // I and dI/dV pair tables (none in exact mode)
            + (size_t)2 * opad * kBwdKT * 4           // dW accumulator
            + (size_t)3 * kBwdMT * kBwdKT * 4         // x, 1/d, -1/(vsat d^2): k-major [4][64]
            + (size_t)2 * 32 * 8 * 4                  // double-buffered chunk thresholds
@@ -582,8 +633,13 @@ __device__ __forceinline__ void bwd_chunk(const float* __restrict__ Xk, const fl
 #pragma unroll
         for (int ip = 0; ip < 4; ++ip) {
             f32x2 pb, pd, nb, nd;
-            lut_bwd2<kClamp, kStride>(X[ip], WP, c, pb, pd);
-            lut_bwd2<kClamp, kStride>(X[ip], WN, c, nb, nd);
+            if (kStride == 0) {  // exact formula
+                exact_bwd2(X[ip], WP, c, pb, pd);
+                exact_bwd2(X[ip], WN, c, nb, nd);
+            } else {
+                lut_bwd2<kClamp, kStride>(X[ip], WP, c, pb, pd);
+                lut_bwd2<kClamp, kStride>(X[ip], WN, c, nb, nd);
+            }
             // d(I_diff/d)/dx = (dp - dn)/d - (bp - bn)/(v_sat d^2)
             const f32x2 e = fma2(sub2(pb, nb), NT[ip], mul2(sub2(pd, nd), IV[ip]));
             dx[ip][kk] = fma2(G[ip], e, dx[ip][kk]);
@@ -640,6 +696,11 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
     lc.dmin2 = pk2(p.dmin, p.dmin);
     lc.scale2 = pk2(p.scale, p.scale);
     lc.two23 = pk2(kTwo23, kTwo23);
+    lc.inv = p.inv;
+    lc.vd = p.vd;
+    lc.i_s = p.i_s;
+    lc.di_s = p.di_s;
+    lc.kappa = p.kappa;
 
     // Threshold range of this CTA's inputs over all outputs (pads count as 0).
     float4 wr;
@@ -677,7 +738,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
         float4 xr;
         bool xnan;
         block_range4(make_float4(xval, xval, INFINITY, -INFINITY), xval != xval, red, red_nan, xr, xnan);
-        const bool fast = tile_in_table(xr.x, xr.y, wr.z, wr.w, xnan || wnan, p.dmin, p.scale, T);
+        const bool fast = kStride == 0 || tile_in_table(xr.x, xr.y, wr.z, wr.w, xnan || wnan, p.dmin, p.scale, T);
 
         f32x2 dx2[4][kBwdKT];  // [token pair][input]
 #pragma unroll
@@ -843,14 +904,16 @@ struct BwdPlan {
     size_t smem, workspace;
 };
 
-int plan_backward(int M, int K, int O, int T, BwdPlan* plan) {
+// stride: table stride of the kernel instance (0 = exact formula, no table);
+// negative selects the LUT stride for T.
+int plan_backward(int M, int K, int O, int T, BwdPlan* plan, int stride = -1) {
     int dev, sms, optin;
     int rc = current_device(&dev);
     if (rc) return rc;
     if ((rc = device_limits(dev, &sms, &optin))) return rc;
     plan->kblocks = (K + kBwdKT - 1) / kBwdKT;
     plan->tiles_m = (M + kBwdMT - 1) / kBwdMT;
-    plan->smem = bwd_smem_bytes(T, O);
+    plan->smem = bwd_smem_bytes_stride(stride < 0 ? bwd_stride(T) : stride, O);
     if (plan->smem > (size_t)optin) {
         return set_error(CIMEKV_ELUT_TOO_LARGE,
                          "backward needs %zu B of shared memory (LUT size %d, out_features %d); device allows %d",
@@ -921,25 +984,42 @@ int cimekv_lut_pack(const uint16_t* table_i, const uint16_t* table_ddelta, int t
     return check_launch("lut_pack_kernel");
 }
 
+struct ExactArgs {
+    float inv, vd, i_s, di_s, kappa;
+};
+
+ExactArgs exact_args(float inv_2nut, float v_d, float i_s) {
+    ExactArgs e;
+    e.inv = inv_2nut;
+    e.vd = v_d;
+    e.i_s = i_s;
+    e.di_s = (float)(2.0 * (double)inv_2nut * (double)i_s);
+    e.kappa = (float)exp(-(double)v_d * (double)inv_2nut);
+    return e;
+}
+
+// ex == nullptr: LUT path; otherwise the exact EKV formula (no table).
 static int launch_forward(const float* x, const float* wpos, const float* wneg, const void* lut, int M, int K,
                           int O, int table_size, float delta_min, float delta_scale, float v_sat, float out_min,
                           float out_max, float* out, const float* r_tia, float tia_lo, float tia_hi, float* tia_out,
-                          void* stream) {
+                          void* stream, const ExactArgs* ex = nullptr) {
     g_last_error[0] = '\0';
-    int rc = check_lut_size(table_size);
+    int rc = ex ? CIMEKV_OK : check_lut_size(table_size);
     if (rc) return rc;
     if (M < 0 || K < 0 || O < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative size M=%d K=%d O=%d", M, K, O);
     if (M == 0 || O == 0) return CIMEKV_OK;
-    if (!lut || !out || (K > 0 && (!x || !wpos || !wneg)) || (tia_out && !r_tia))
+    if ((!lut && !ex) || !out || (K > 0 && (!x || !wpos || !wneg)) || (tia_out && !r_tia))
         return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
-    if (!aligned16(lut)) return set_error(CIMEKV_EINVAL_SHAPE, "lut must be 16-byte aligned");
-    if (!(delta_scale > 0.0f)) return set_error(CIMEKV_EINVAL_SHAPE, "delta_scale must be > 0");
+    if (!ex && !aligned16(lut)) return set_error(CIMEKV_EINVAL_SHAPE, "lut must be 16-byte aligned");
+    if (!ex && !(delta_scale > 0.0f)) return set_error(CIMEKV_EINVAL_SHAPE, "delta_scale must be > 0");
+    if (ex) table_size = 0;
     int dev, sms, optin;
     if ((rc = current_device(&dev))) return rc;
     if ((rc = device_limits(dev, &sms, &optin))) return rc;
     const size_t smem = fwd_smem_bytes(table_size);
     if (smem > (size_t)optin) return set_error(CIMEKV_ELUT_TOO_LARGE, "forward needs %zu B shared memory", smem);
-    if ((rc = allow_smem(dev, 0, fwd_kernel, optin))) return rc;
+    if ((rc = ex ? allow_smem(dev, 4, fwd_kernel<true>, optin) : allow_smem(dev, 0, fwd_kernel<false>, optin)))
+        return rc;
     FwdParams p;
     p.x = x;
     p.wp = wpos;
@@ -959,13 +1039,19 @@ static int launch_forward(const float* x, const float* wpos, const float* wneg, 
     p.tia_out = tia_out;
     p.tia_lo = tia_lo;
     p.tia_hi = tia_hi;
+    p.inv = ex ? ex->inv : 0.0f;
+    p.vd = ex ? ex->vd : 0.0f;
+    p.i_s = ex ? ex->i_s : 0.0f;
+    p.di_s = ex ? ex->di_s : 0.0f;
+    p.kappa = ex ? ex->kappa : 0.0f;
     const long ntiles = (long)((M + kFwdMT - 1) / kFwdMT) * ((O + kFwdOT - 1) / kFwdOT);
     int resident = (int)((228 * 1024) / (smem + 1024));
     if (resident > CIMEKV_FWD_MIN_BLOCKS) resident = CIMEKV_FWD_MIN_BLOCKS;
     if (resident < 1) resident = 1;
     long grid = (long)sms * resident;
     if (grid > ntiles) grid = ntiles;
-    fwd_kernel<<<(unsigned)grid, kFwdThreads, smem, (cudaStream_t)stream>>>(p);
+    if (ex) fwd_kernel<true><<<(unsigned)grid, kFwdThreads, smem, (cudaStream_t)stream>>>(p);
+    else fwd_kernel<false><<<(unsigned)grid, kFwdThreads, smem, (cudaStream_t)stream>>>(p);
     return check_launch("fwd_kernel");
 }
 
@@ -1218,6 +1304,93 @@ extern "C" int cimekv_backward_noalloc(const float* x, const float* wpos, const 
     else if (stride == 8192) bwd_kernel<8192><<<grid, kBwdThreads, plan.smem, s>>>(p);
     else bwd_kernel<16384><<<grid, kBwdThreads, plan.smem, s>>>(p);
     if ((rc = check_launch("bwd_kernel"))) return rc;
+    if (want_w) {
+        const int64_t n = (int64_t)O * K;
+        int blocks = (int)((n + 255) / 256);
+        if (blocks > sms * 8) blocks = sms * 8;
+        bwd_reduce_kernel<<<blocks, 256, 0, s>>>(p.part, plan.nsplit, n, grad_wpos, grad_wneg);
+        if ((rc = check_launch("bwd_reduce_kernel"))) return rc;
+    }
+    return CIMEKV_OK;
+}
+
+// ==================================================== exact-formula path ==
+
+extern "C" int cimekv_exact_forward(const float* x, const float* wpos, const float* wneg, int M, int K, int O,
+                                    float inv_2nut, float v_d, float i_s, float v_sat, float* out, void* stream) {
+    const ExactArgs ex = exact_args(inv_2nut, v_d, i_s);
+    return launch_forward(x, wpos, wneg, nullptr, M, K, O, 0, 0.0f, 1.0f, v_sat, -INFINITY, INFINITY, out, nullptr,
+                          0.0f, 0.0f, nullptr, stream, &ex);
+}
+
+extern "C" size_t cimekv_exact_backward_workspace_bytes(int M, int K, int O) {
+    if (M <= 0 || K <= 0 || O <= 0) return 0;
+    BwdPlan plan;
+    if (plan_backward(M, K, O, 0, &plan, 0)) return 0;
+    return plan.workspace;
+}
+
+extern "C" int cimekv_exact_backward(const float* x, const float* wpos, const float* wneg, const float* grad_out,
+                                     int M, int K, int O, float inv_2nut, float v_d, float i_s, float v_sat,
+                                     float* grad_x, float* grad_wpos, float* grad_wneg, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+    g_last_error[0] = '\0';
+    if (M < 0 || K < 0 || O < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative size M=%d K=%d O=%d", M, K, O);
+    if ((grad_wpos == nullptr) != (grad_wneg == nullptr))
+        return set_error(CIMEKV_EINVAL_SHAPE, "grad_wpos and grad_wneg must both be given or both be NULL");
+    const bool want_w = grad_wpos != nullptr;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (K == 0) return CIMEKV_OK;
+    if (M == 0 || O == 0) {
+        if (want_w && O > 0) {
+            fill_zero_kernel<<<64, 256, 0, s>>>(grad_wpos, (int64_t)O * K);
+            fill_zero_kernel<<<64, 256, 0, s>>>(grad_wneg, (int64_t)O * K);
+        }
+        if (grad_x && M > 0) fill_zero_kernel<<<64, 256, 0, s>>>(grad_x, (int64_t)M * K);
+        return check_launch("fill_zero_kernel");
+    }
+    if (!grad_x && !want_w) return CIMEKV_OK;
+    if (!x || !wpos || !wneg || !grad_out) return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
+    BwdPlan plan;
+    int rc;
+    if ((rc = plan_backward(M, K, O, 0, &plan, 0))) return rc;
+    if (want_w) {
+        if (!workspace || workspace_bytes < plan.workspace)
+            return set_error(CIMEKV_EWORKSPACE, "backward workspace needs %zu B, got %zu B", plan.workspace,
+                             workspace_bytes);
+        if (!aligned16(workspace)) return set_error(CIMEKV_EINVAL_SHAPE, "workspace must be 16-byte aligned");
+    }
+    int dev, sms, optin;
+    if ((rc = current_device(&dev))) return rc;
+    if ((rc = device_limits(dev, &sms, &optin))) return rc;
+    if ((rc = allow_smem(dev, 5, bwd_kernel<0>, optin))) return rc;
+    const ExactArgs ex = exact_args(inv_2nut, v_d, i_s);
+    BwdParams p;
+    p.x = x;
+    p.wp = wpos;
+    p.wn = wneg;
+    p.g = grad_out;
+    p.lut_i = nullptr;
+    p.lut_d = nullptr;
+    p.grad_x = grad_x;
+    p.part = want_w ? static_cast<float*>(workspace) : nullptr;
+    p.M = M;
+    p.K = K;
+    p.O = O;
+    p.T = 0;
+    p.tiles_m = plan.tiles_m;
+    p.nsplit = plan.nsplit;
+    p.dmin = 0.0f;
+    p.scale = 1.0f;
+    p.vsat = v_sat;
+    p.inv = ex.inv;
+    p.vd = ex.vd;
+    p.i_s = ex.i_s;
+    p.di_s = ex.di_s;
+    p.kappa = ex.kappa;
+    dim3 grid(plan.kblocks, plan.nsplit);
+    bwd_kernel<0><<<grid, kBwdThreads, plan.smem, s>>>(p);
+    if ((rc = check_launch("bwd_kernel<exact>"))) return rc;
     if (want_w) {
         const int64_t n = (int64_t)O * K;
         int blocks = (int)((n + 255) / 256);

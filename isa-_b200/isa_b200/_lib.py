@@ -39,6 +39,11 @@ SIGNATURES = {
                                  _c_float, _c_float, _c_float, _vp, _vp, _vp, _vp, _c_size, _vp]),
     "cimekv_backward_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
                                          _c_float, _c_float, _c_float, _vp, _vp, _vp, _vp]),
+    "cimekv_exact_forward": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_float, _c_float, _c_float,
+                                      _c_float, _vp, _vp]),
+    "cimekv_exact_backward_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int]),
+    "cimekv_exact_backward": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_float, _c_float, _c_float,
+                                       _c_float, _vp, _vp, _vp, _vp, _c_size, _vp]),
     "cimekv_lut_index": (_c_int, [_vp, _c_int, _c_int, _c_float, _c_float, _vp, _vp, _vp]),
     "cimekv_fp32_probe": (_c_int, [_vp, _c_int, _c_int, ctypes.POINTER(ctypes.c_longlong), _vp]),
 }
@@ -163,6 +168,29 @@ def backward_noalloc(x, wpos, wneg, grad_out, lut, table_size, delta_min, delta_
                                         int(table_size), delta_min, delta_scale, v_sat,
                                         _ptr(grad_x), _ptr(grad_wpos), _ptr(grad_wneg), _stream(stream))
     _check(rc, "cimekv_backward_noalloc")
+
+
+def exact_forward(x, wpos, wneg, inv_2nut, v_d, i_s, v_sat, out, stream=None) -> None:
+    m, k = x.shape
+    o = wpos.shape[0]
+    rc = load().cimekv_exact_forward(_ptr(x), _ptr(wpos), _ptr(wneg), m, k, o, inv_2nut, v_d, i_s, v_sat,
+                                     _ptr(out), _stream(stream))
+    _check(rc, "cimekv_exact_forward")
+
+
+def exact_backward_workspace_bytes(m: int, k: int, o: int) -> int:
+    return int(load().cimekv_exact_backward_workspace_bytes(int(m), int(k), int(o)))
+
+
+def exact_backward(x, wpos, wneg, grad_out, inv_2nut, v_d, i_s, v_sat, grad_x, grad_wpos, grad_wneg, workspace,
+                   stream=None) -> None:
+    m, k = x.shape
+    o = wpos.shape[0]
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = load().cimekv_exact_backward(_ptr(x), _ptr(wpos), _ptr(wneg), _ptr(grad_out), m, k, o,
+                                      inv_2nut, v_d, i_s, v_sat, _ptr(grad_x), _ptr(grad_wpos), _ptr(grad_wneg),
+                                      _ptr(workspace), ws_bytes, _stream(stream))
+    _check(rc, "cimekv_exact_backward")
 
 
 def lut_index(delta: torch.Tensor, table_size: int, delta_min: float, delta_scale: float,

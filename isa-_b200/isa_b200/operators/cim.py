@@ -21,6 +21,7 @@ import torch
 import torch.nn as nn
 
 from isa_b200.device_models.config import FLASH_TRANSISTOR_EKV_CONFIG as PHYSICAL_CONFIG
+from isa_b200.kernels.transformer_ffn.ekv_exact import cuda_ekv_matmul
 from isa_b200.kernels.transformer_ffn.ekv_lut import cuda_lut_ekv_matmul, cuda_lut_ekv_matmul_tia
 
 
@@ -48,12 +49,10 @@ def clamp_signed(v: torch.Tensor, v_min: float = -4.0, v_max: float = 4.0) -> to
     return v.clamp(v_min, v_max)
 
 
-def _lut_approx(cfg: Dict) -> None:
-    approx = str(cfg.get("ekv_approx", "lut")).lower()
-    if approx != "lut":
-        raise NotImplementedError(
-            f"ekv_approx={approx!r}: only the LUT path ('lut') is implemented on sm_100a"
-        )
+def _uses_lut(cfg: Dict) -> bool:
+    """The reference dispatch (cim.py:183-186): 'lut' -> LUT kernels, anything
+    else -> exact-formula kernels."""
+    return str(cfg.get("ekv_approx", "lut")).lower() == "lut"
 
 
 class CIMLinear(nn.Module):
@@ -150,20 +149,26 @@ class CIMLinear(nn.Module):
     @torch.no_grad()
     def estimate_idiff(self, x: torch.Tensor, max_rows: int = 4096) -> torch.Tensor:
         """I_diff of the first ``max_rows`` rows, without TIA (reference ``cim.py:140-163``)."""
-        _lut_approx(self.cfg)
         flat = x.reshape(-1, self.in_features)
         flat = flat[:max_rows].contiguous()
-        return cuda_lut_ekv_matmul(flat, self.vth_pos, self.vth_neg, self.cfg)
+        if _uses_lut(self.cfg):
+            return cuda_lut_ekv_matmul(flat, self.vth_pos, self.vth_neg, self.cfg)
+        return cuda_ekv_matmul(flat, self.vth_pos, self.vth_neg, self.cfg)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         b, n, in_f = x.shape
         if in_f != self.in_features:
             raise ValueError(f"expected {self.in_features} input features, got {in_f}")
-        _lut_approx(self.cfg)
-        # I_diff, * R_TIA and the signed clamp in one fused kernel (reference:
-        # LUT matmul, then `* r_tia` and `clamp` in torch).
         r_tia = self.r_tia.to(device=x.device, dtype=torch.float32)
-        out = cuda_lut_ekv_matmul_tia(x.reshape(b * n, in_f), self.vth_pos, self.vth_neg, r_tia, self.cfg)
+        flat = x.reshape(b * n, in_f)
+        if _uses_lut(self.cfg):
+            # I_diff, * R_TIA and the signed clamp in one fused kernel (reference:
+            # LUT matmul, then `* r_tia` and `clamp` in torch).
+            out = cuda_lut_ekv_matmul_tia(flat, self.vth_pos, self.vth_neg, r_tia, self.cfg)
+        else:
+            v_lo = float(self.cfg.get("V_signed_min", -4.0))
+            v_hi = float(self.cfg.get("V_signed_max", 4.0))
+            out = (cuda_ekv_matmul(flat, self.vth_pos, self.vth_neg, self.cfg) * r_tia).clamp(v_lo, v_hi)
         out = out.view(b, n, self.out_features)
         if self.track_output_stats:
             with torch.no_grad():

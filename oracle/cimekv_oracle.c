@@ -189,3 +189,92 @@ void oracle_backward(const float* x, const float* wp, const float* wn, const flo
         }
     }
 }
+
+/* ------------------------------------------------------------------------
+ * Exact-formula path (cfg ekv_approx != "lut"), in fp64.
+ * Follows the reference's CPU formulation, src/isa/device_models/
+ * flash_transistor.py:27-82 (ekv_current, ekv_current_grad_v,
+ * ekv_current_grad_vth; torch softplus with threshold 20), which its exact
+ * Triton kernels (src/isa/kernels/transformer_ffn/ekv_triton.py:23-150)
+ * evaluate in fp32.  Magnitudes sum |I_pos| + |I_neg| per term, because the two
+ * branches are evaluated independently and their fp32 errors do not cancel.
+ * ------------------------------------------------------------------------ */
+static inline double sp_exact(double u) { return u > 20.0 ? u : log1p(exp(u)); }
+static inline double sig_exact(double u) { return 1.0 / (1.0 + exp(-u)); }
+
+/* I_S (sp1^2 - sp2^2) and its derivative in dV (without the 1/(1+V/V_sat) factor). */
+static inline void ekv_exact(double dv, double inv, double vd, double is, double* I, double* dI) {
+    const double u1 = dv * inv, u2 = (dv - vd) * inv;
+    const double s1 = sp_exact(u1), s2 = sp_exact(u2);
+    *I = is * (s1 * s1 - s2 * s2);
+    if (dI) *dI = is * 2.0 * inv * (s1 * sig_exact(u1) - s2 * sig_exact(u2));
+}
+
+void oracle_exact_forward(const float* x, const float* wp, const float* wn, int M, int K, int O, double inv,
+                          double vd, double is, double v_sat, float* out, float* mag, int nthreads) {
+    set_threads(nthreads);
+#pragma omp parallel for schedule(static)
+    for (long mo = 0; mo < (long)M * O; ++mo) {
+        const long m = mo / O, o = mo % O;
+        double acc = 0.0, am = 0.0;
+        for (int k = 0; k < K; ++k) {
+            const double xv = x[m * K + k];
+            double ip, in_;
+            ekv_exact(xv - (double)wp[o * K + k], inv, vd, is, &ip, NULL);
+            ekv_exact(xv - (double)wn[o * K + k], inv, vd, is, &in_, NULL);
+            const double d = 1.0 + xv / v_sat;
+            acc += (ip - in_) / d;
+            am += (fabs(ip) + fabs(in_)) / fabs(d);
+        }
+        out[mo] = (float)acc;
+        if (mag) mag[mo] = (float)am;
+    }
+}
+
+void oracle_exact_backward(const float* x, const float* wp, const float* wn, const float* g, int M, int K, int O,
+                           double inv, double vd, double is, double v_sat, float* grad_x, float* grad_wp,
+                           float* grad_wn, float* mag_x, float* mag_wp, float* mag_wn, int nthreads) {
+    set_threads(nthreads);
+    if (grad_x) {
+#pragma omp parallel for schedule(static)
+        for (long mk = 0; mk < (long)M * K; ++mk) {
+            const long m = mk / K, k = mk % K;
+            const double xv = x[mk];
+            const double d = 1.0 + xv / v_sat;
+            double acc = 0.0, am = 0.0;
+            for (int o = 0; o < O; ++o) {
+                double ip, dip, in_, din;
+                ekv_exact(xv - (double)wp[(long)o * K + k], inv, vd, is, &ip, &dip);
+                ekv_exact(xv - (double)wn[(long)o * K + k], inv, vd, is, &in_, &din);
+                const double gv = g[m * O + o];
+                acc += gv * ((dip - din) / d - (ip - in_) / (v_sat * d * d));
+                am += fabs(gv) * ((fabs(dip) + fabs(din)) / fabs(d) + (fabs(ip) + fabs(in_)) / (v_sat * d * d));
+            }
+            grad_x[mk] = (float)acc;
+            if (mag_x) mag_x[mk] = (float)am;
+        }
+    }
+    if (grad_wp || grad_wn) {
+#pragma omp parallel for schedule(static)
+        for (long ok = 0; ok < (long)O * K; ++ok) {
+            const long o = ok / K, k = ok % K;
+            double ap = 0.0, an = 0.0, mp = 0.0, mn = 0.0;
+            for (int m = 0; m < M; ++m) {
+                const double xv = x[(long)m * K + k];
+                const double gv = g[(long)m * O + o];
+                const double d = 1.0 + xv / v_sat;
+                double ip, dip, in_, din;
+                ekv_exact(xv - (double)wp[ok], inv, vd, is, &ip, &dip);
+                ekv_exact(xv - (double)wn[ok], inv, vd, is, &in_, &din);
+                ap += gv * (-dip / d);
+                an += gv * (din / d);
+                mp += fabs(gv * dip / d);
+                mn += fabs(gv * din / d);
+            }
+            if (grad_wp) grad_wp[ok] = (float)ap;
+            if (grad_wn) grad_wn[ok] = (float)an;
+            if (mag_wp) mag_wp[ok] = (float)mp;
+            if (mag_wn) mag_wn[ok] = (float)mn;
+        }
+    }
+}

@@ -37,6 +37,9 @@ def load() -> ctypes.CDLL:
         lib.oracle_forward.argtypes = [vp, vp, vp, vp, i, i, i, i, f, f, f, f, f, vp, vp, i]
         lib.oracle_backward.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, f, f, f,
                                         vp, vp, vp, vp, vp, vp, i]
+        d = ctypes.c_double
+        lib.oracle_exact_forward.argtypes = [vp, vp, vp, i, i, i, d, d, d, d, vp, vp, i]
+        lib.oracle_exact_backward.argtypes = [vp, vp, vp, vp, i, i, i, d, d, d, d, vp, vp, vp, vp, vp, vp, i]
         _lib = lib
     return _lib
 
@@ -97,6 +100,40 @@ def backward(x, wp, wn, g, table_i, table_dd, delta_min, scale, v_sat, need_x=Tr
     load().oracle_backward(_p(x), _p(wp), _p(wn), _p(g), _p(ti), _p(td), m, k, o, ti.size, float(delta_min),
                            float(scale), float(v_sat), _p(gx), _p(gwp), _p(gwn), _p(mx), _p(mwp), _p(mwn),
                            int(nthreads))
+    if with_mag:
+        return (gx, gwp, gwn), (mx, mwp, mwn)
+    return gx, gwp, gwn
+
+
+def exact_consts(cfg) -> tuple[float, float, float, float]:
+    """(1/(2 n U_T), V_D, I_S, V_sat) of a cfg dict, as the reference computes them."""
+    return 1.0 / (2.0 * float(cfg["n"]) * float(cfg["U_T"])), float(cfg["V_D"]), float(cfg["I_S"]), float(cfg["V_sat"])
+
+
+def exact_forward(x, wp, wn, inv, vd, i_s, v_sat, nthreads=0, with_mag=False):
+    """Exact-formula forward in fp64 (flash_transistor.py:27-41 semantics)."""
+    x, wp, wn = _f32(x), _f32(wp), _f32(wn)
+    m, k = x.shape
+    o = wp.shape[0]
+    out = np.empty((m, o), np.float32)
+    mag = np.empty((m, o), np.float32) if with_mag else None
+    load().oracle_exact_forward(_p(x), _p(wp), _p(wn), m, k, o, inv, vd, i_s, v_sat, _p(out), _p(mag), int(nthreads))
+    return (out, mag) if with_mag else out
+
+
+def exact_backward(x, wp, wn, g, inv, vd, i_s, v_sat, need_x=True, need_w=True, nthreads=0, with_mag=False):
+    """Exact-formula gradients in fp64 (flash_transistor.py:44-82 semantics)."""
+    x, wp, wn, g = _f32(x), _f32(wp), _f32(wn), _f32(g)
+    m, k = x.shape
+    o = wp.shape[0]
+    gx = np.empty((m, k), np.float32) if need_x else None
+    gwp = np.empty((o, k), np.float32) if need_w else None
+    gwn = np.empty((o, k), np.float32) if need_w else None
+    mx = np.empty((m, k), np.float32) if (with_mag and need_x) else None
+    mwp = np.empty((o, k), np.float32) if (with_mag and need_w) else None
+    mwn = np.empty((o, k), np.float32) if (with_mag and need_w) else None
+    load().oracle_exact_backward(_p(x), _p(wp), _p(wn), _p(g), m, k, o, inv, vd, i_s, v_sat, _p(gx), _p(gwp),
+                                 _p(gwn), _p(mx), _p(mwp), _p(mwn), int(nthreads))
     if with_mag:
         return (gx, gwp, gwn), (mx, mwp, mwn)
     return gx, gwp, gwn

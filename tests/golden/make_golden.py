@@ -167,6 +167,26 @@ def main(ref_root: str) -> None:
                         table_ddelta=td.view(torch.int16).numpy().view(np.uint16))
     print("builder golden saved")
 
+    # 8. Exact-formula path: the reference's exact Triton kernels
+    #    (ekv_triton.py:69-150, TritonEKVMatmulFn) on two small cases.
+    from isa.kernels.transformer_ffn import ekv_triton as ref_exact
+    for name, (m, k, o), lo, hi in (("exact_small", (32, 48, 40), -1.0, 1.0),
+                                    ("exact_ragged", (19, 37, 45), -4.0, 4.0)):
+        cfg = cfg_for(4096)
+        x = rng.uniform(lo, hi, (m, k)).astype(np.float32) + 2.5
+        wp, wn = vth_init(o, k, 7, 8, cfg)
+        g = rng.standard_normal((m, o)).astype(np.float32)
+        xt = torch.from_numpy(x).requires_grad_(True)
+        pt = torch.from_numpy(wp).requires_grad_(True)
+        nt = torch.from_numpy(wn).requires_grad_(True)
+        out = ref_exact.triton_ekv_matmul(xt, pt, nt, cfg)
+        out.backward(torch.from_numpy(g))
+        np.savez_compressed(HERE / f"golden_{name}.npz", x=x, wpos=wp, wneg=wn, grad_out=g,
+                            out=out.detach().numpy(), grad_x=xt.grad.numpy(), grad_wpos=pt.grad.numpy(),
+                            grad_wneg=nt.grad.numpy(), n=np.float64(cfg["n"]), U_T=np.float64(cfg["U_T"]),
+                            V_D=np.float64(cfg["V_D"]), I_S=np.float64(cfg["I_S"]), V_sat=np.float64(cfg["V_sat"]))
+        print(f"{name} saved")
+
 
 if __name__ == "__main__":
     main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

@@ -82,3 +82,17 @@ def test_lut_builder_matches_formula_loosely():
     inv = 1.0 / (2.0 * n * u_t)
     expected = i_s * (F.softplus(delta * inv).square() - F.softplus((delta - v_d) * inv).square())
     assert torch.allclose(table.float(), expected, rtol=8.0e-3, atol=3.0e-3)
+
+
+@pytest.mark.parametrize("case", ["exact_small", "exact_ragged"])
+def test_exact_oracle_matches_reference_exact_triton(case):
+    g = load_golden(case)
+    inv = 1.0 / (2.0 * float(g["n"]) * float(g["U_T"]))
+    args = (inv, float(g["V_D"]), float(g["I_S"]), float(g["V_sat"]))
+    out, mag = oracle.exact_forward(g["x"], g["wpos"], g["wneg"], *args, with_mag=True)
+    assert_close_scaled(out, g["out"], mag, what=f"{case} exact forward")
+    (gx, gwp, gwn), (mx, mwp, mwn) = oracle.exact_backward(g["x"], g["wpos"], g["wneg"], g["grad_out"], *args,
+                                                           with_mag=True)
+    assert_close_scaled(gx, g["grad_x"], mx, what=f"{case} exact grad_x")
+    assert_close_scaled(gwp, g["grad_wpos"], mwp, what=f"{case} exact grad_wpos")
+    assert_close_scaled(gwn, g["grad_wneg"], mwn, what=f"{case} exact grad_wneg")
