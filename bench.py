@@ -41,6 +41,10 @@ WORKLOADS = {
     # Config 3 with the exact-formula path (cfg ekv_approx="exact"; the LUT is the default)
     "gpt_m_ffn_exact": dict(model="Physical GPT-M FFN block, exact EKV formula", d=384, hidden=1536, batch=32,
                             seq=1024, lut=4096, approx="exact"),
+    # Measured-codebook fc1 (DeploymentAwareCIMLinear "measured" mode) at the ViT-L fc1 shape:
+    # 256 images x 197 tokens, 384 -> 1536, 24 measured curves on a 33-point Vg grid
+    "vit_l_fc1_measured": dict(model="ViT-L fc1, measured 24-state codebook", d=384, hidden=1536, batch=256,
+                               seq=197, lut=8192, measured=True),
     # Physical GPT-L full training step, global batch 64 x 1024 (strong scaling)
     "gpt_l_step": dict(model="Physical GPT-L (d=768, ffn 3072, 12 layers, 12 heads, vocab 50257)", d=768,
                        hidden=3072, batch=64, seq=1024, lut=4096, layers=12),
@@ -550,9 +554,64 @@ def run_gpt_l(args, wl):
         dist.destroy_process_group()
 
 
+def run_measured(args, wl):
+    """fc1 in measured mode: forward (per-cell codebook gather, fused TIA) and
+    input gradient; the reference arm runs its own module (masked GEMM per
+    active segment, measured_deployment/operator.py:163-206)."""
+    import numpy as np
+    import torch
+
+    ref = args.impl == "reference_gpu"
+    if ref:
+        sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+        from isa.measured_deployment.operator import DeploymentAwareCIMLinear
+    else:
+        from isa_b200.operators.measured import DeploymentAwareCIMLinear
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rng = np.random.default_rng(0)
+    torch.manual_seed(0)
+    layer = DeploymentAwareCIMLinear(wl["d"], wl["hidden"]).to(dev)
+    layer.set_r_tia(2.0e4)
+    g_pts = 33
+    vg = np.linspace(-0.5, 4.5, g_pts).astype(np.float32)
+    cur = (np.exp(rng.uniform(-14, -11, (24, 1))) * np.cumsum(rng.uniform(0, 1, (24, g_pts)), axis=1)).astype(np.float32)
+    layer.configure_codebook(torch.from_numpy(vg), torch.from_numpy(cur))
+    pos = torch.from_numpy(rng.integers(0, 24, (wl["hidden"], wl["d"])).astype(np.int16))
+    neg = torch.from_numpy(rng.integers(0, 24, (wl["hidden"], wl["d"])).astype(np.int16))
+    layer.set_assignment(pos, neg)
+    layer.set_forward_mode("measured")
+    x = (torch.rand(wl["batch"], wl["seq"], wl["d"], device=dev) * 4.0).requires_grad_(True)
+    g = torch.randn(wl["batch"], wl["seq"], wl["hidden"], device=dev)
+
+    def step():
+        x.grad = None
+        layer(x).backward(g)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_.record()
+    for _ in range(args.steps):
+        step()
+    e_.record()
+    e_.synchronize()
+    ms = s_.elapsed_time(e_) / args.steps
+    cells = wl["batch"] * wl["seq"] * wl["d"] * wl["hidden"]
+    print(json.dumps({"metric": "measured fc1 fwd+dX Gcell-evals/s", "value": cells / (ms * 1e-3) / 1e9,
+                      "unit": "Gcell-evals/s", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+                      "impl": args.impl, "config": {"workload": args.workload, "tokens": wl["batch"] * wl["seq"],
+                                                    "d": wl["d"], "hidden": wl["hidden"], "states": 24,
+                                                    "grid_points": g_pts}}), flush=True)
+
+
 def main():
     args = parse()
     wl = WORKLOADS[args.workload]
+    if wl.get("measured"):
+        run_measured(args, wl)
+        return
     if args.workload == "gpt_l_step":
         if args.impl != "ours":
             raise SystemExit("gpt_l_step is measured for this build only")

@@ -144,6 +144,35 @@ int cimekv_exact_backward(const float* x, const float* wpos, const float* wneg,
                           void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Measured-codebook forward (DeploymentAwareCIMLinear "measured" mode,
+ * src/isa/measured_deployment/operator.py:163-206; its fused Triton kernel
+ * measured_deployment/kernels/measured_lut_triton.py:24-...).  Each device
+ * (o,k) uses measured curve pos_idx[o,k] / neg_idx[o,k] (int16, S states); a
+ * curve is piecewise linear over the strictly increasing grid vg[G], with
+ * coef[s][j] = {slope, intercept} on segment j.  With x clamped to
+ * [lookup_min, lookup_max] and j = searchsorted(vg, x, right) - 1:
+ *   idiff[m,o] = sum_k x (a_p - a_n) + (b_p - b_n)       (may be NULL)
+ *   out[m,o]   = clamp(idiff * (*r_tia), out_min, out_max)
+ * S*(G-1) <= 16384.  r_tia is a device scalar.
+ */
+int cimekv_measured_forward(const float* x, const int16_t* pos_idx, const int16_t* neg_idx,
+                            const float* vg, const float* coef, int M, int K, int O, int S, int G,
+                            float lookup_min, float lookup_max, const float* r_tia,
+                            float out_min, float out_max, float* idiff, float* out, void* stream);
+
+/*
+ * Input gradient of cimekv_measured_forward (the curves are fixed buffers, so
+ * there is no threshold gradient; r_tia is detached as in the reference):
+ *   grad_x[m,k] = [lookup_min <= x <= lookup_max]
+ *                 * sum_o g[m,o] r [out_min <= idiff r <= out_max] (a_p - a_n)[j(x)]
+ */
+int cimekv_measured_backward_x(const float* x, const int16_t* pos_idx, const int16_t* neg_idx,
+                               const float* vg, const float* coef, int M, int K, int O, int S, int G,
+                               float lookup_min, float lookup_max, const float* r_tia,
+                               float out_min, float out_max, const float* idiff,
+                               const float* grad_out, float* grad_x, void* stream);
+
+/*
  * Index selection of one lookup, for parity tests: for each dV in delta[n],
  * writes the table entry i0 the kernels use and the interpolation weight a,
  * computed by the same device code as the forward and backward

@@ -55,6 +55,12 @@ int set_error(int code, const char* fmt, ...) {
     return code;
 }
 
+}  // namespace
+
+void cimekv_internal_set_error(const char* msg) { snprintf(g_last_error, sizeof(g_last_error), "%s", msg); }
+
+namespace {
+
 int check_launch(const char* what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {

@@ -44,6 +44,10 @@ SIGNATURES = {
     "cimekv_exact_backward_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int]),
     "cimekv_exact_backward": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_float, _c_float, _c_float,
                                        _c_float, _vp, _vp, _vp, _vp, _c_size, _vp]),
+    "cimekv_measured_forward": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                         _c_float, _c_float, _vp, _c_float, _c_float, _vp, _vp, _vp]),
+    "cimekv_measured_backward_x": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                            _c_float, _c_float, _vp, _c_float, _c_float, _vp, _vp, _vp, _vp]),
     "cimekv_lut_index": (_c_int, [_vp, _c_int, _c_int, _c_float, _c_float, _vp, _vp, _vp]),
     "cimekv_fp32_probe": (_c_int, [_vp, _c_int, _c_int, ctypes.POINTER(ctypes.c_longlong), _vp]),
 }
@@ -191,6 +195,28 @@ def exact_backward(x, wpos, wneg, grad_out, inv_2nut, v_d, i_s, v_sat, grad_x, g
                                       inv_2nut, v_d, i_s, v_sat, _ptr(grad_x), _ptr(grad_wpos), _ptr(grad_wneg),
                                       _ptr(workspace), ws_bytes, _stream(stream))
     _check(rc, "cimekv_exact_backward")
+
+
+def measured_forward(x, pos_idx, neg_idx, vg, coef, lookup_min, lookup_max, r_tia, out_min, out_max, idiff, out,
+                     stream=None) -> None:
+    m, k = x.shape
+    o = pos_idx.shape[0]
+    s_, g_ = coef.shape[0], vg.numel()
+    rc = load().cimekv_measured_forward(_ptr(x), _ptr(pos_idx), _ptr(neg_idx), _ptr(vg), _ptr(coef), m, k, o, s_, g_,
+                                        lookup_min, lookup_max, _ptr(r_tia), out_min, out_max, _ptr(idiff), _ptr(out),
+                                        _stream(stream))
+    _check(rc, "cimekv_measured_forward")
+
+
+def measured_backward_x(x, pos_idx, neg_idx, vg, coef, lookup_min, lookup_max, r_tia, out_min, out_max, idiff,
+                        grad_out, grad_x, stream=None) -> None:
+    m, k = x.shape
+    o = pos_idx.shape[0]
+    s_, g_ = coef.shape[0], vg.numel()
+    rc = load().cimekv_measured_backward_x(_ptr(x), _ptr(pos_idx), _ptr(neg_idx), _ptr(vg), _ptr(coef), m, k, o,
+                                           s_, g_, lookup_min, lookup_max, _ptr(r_tia), out_min, out_max,
+                                           _ptr(idiff), _ptr(grad_out), _ptr(grad_x), _stream(stream))
+    _check(rc, "cimekv_measured_backward_x")
 
 
 def lut_index(delta: torch.Tensor, table_size: int, delta_min: float, delta_scale: float,

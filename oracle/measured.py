@@ -1,0 +1,64 @@
+"""fp64 restatement of the measured-codebook forward — TEST INFRASTRUCTURE ONLY.
+
+Follows src/isa/measured_deployment/operator.py: per-segment slopes and
+intercepts (:119-123), clamp of the input to the lookup range and
+right-bisect segment selection (:171-196), sum over inputs of
+x*(slope_p - slope_n) + (icpt_p - icpt_n), then * r_tia and the signed clamp
+(:198-203).  The input gradient is the analytic derivative of that
+piecewise-linear map (what autograd of the reference's masked GEMMs gives).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def coefficients(vg, currents):
+    vg = np.asarray(vg, np.float64)
+    cur = np.asarray(currents, np.float64)
+    slopes = (cur[:, 1:] - cur[:, :-1]) / (vg[1:] - vg[:-1])[None, :]
+    return slopes, cur[:, :-1] - slopes * vg[None, :-1]
+
+
+def forward(x, vg, currents, pos, neg, lookup_min, lookup_max, r_tia, lo=-4.0, hi=4.0):
+    """Returns (out, idiff, mag) with mag = sum |x da| + |db| per output."""
+    x = np.asarray(x, np.float64)
+    a, b = coefficients(vg, currents)
+    xc = np.clip(x, lookup_min, lookup_max)
+    seg = np.clip(np.searchsorted(np.asarray(vg, np.float64), xc, side="right") - 1, 0, len(vg) - 2)
+    pos = np.asarray(pos, np.int64)
+    neg = np.asarray(neg, np.int64)
+    m, k = x.shape
+    o = pos.shape[0]
+    idiff = np.zeros((m, o))
+    mag = np.zeros((m, o))
+    for kk in range(k):
+        s = seg[:, kk][:, None]          # [m,1]
+        da = a[pos[:, kk][None, :], s] - a[neg[:, kk][None, :], s]   # [m,o]
+        db = b[pos[:, kk][None, :], s] - b[neg[:, kk][None, :], s]
+        term = xc[:, kk][:, None] * da + db
+        idiff += term
+        mag += np.abs(xc[:, kk][:, None] * da) + np.abs(db)
+    return np.clip(idiff * r_tia, lo, hi), idiff, mag
+
+
+def backward_x(x, vg, currents, pos, neg, lookup_min, lookup_max, r_tia, grad_out, lo=-4.0, hi=4.0):
+    """(grad_x, mag) of the measured forward."""
+    x = np.asarray(x, np.float64)
+    a, _ = coefficients(vg, currents)
+    _, idiff, _ = forward(x, vg, currents, pos, neg, lookup_min, lookup_max, r_tia, lo, hi)
+    v = idiff * r_tia
+    gm = np.asarray(grad_out, np.float64) * r_tia * ((v >= lo) & (v <= hi))
+    xc = np.clip(x, lookup_min, lookup_max)
+    seg = np.clip(np.searchsorted(np.asarray(vg, np.float64), xc, side="right") - 1, 0, len(vg) - 2)
+    pos = np.asarray(pos, np.int64)
+    neg = np.asarray(neg, np.int64)
+    gx = np.zeros_like(x)
+    mag = np.zeros_like(x)
+    for kk in range(x.shape[1]):
+        s = seg[:, kk][:, None]
+        da = a[pos[:, kk][None, :], s] - a[neg[:, kk][None, :], s]
+        gx[:, kk] = (gm * da).sum(1)
+        mag[:, kk] = np.abs(gm * da).sum(1)
+    inside = (x >= lookup_min) & (x <= lookup_max)
+    return gx * inside, mag

@@ -187,6 +187,34 @@ def main(ref_root: str) -> None:
                             V_D=np.float64(cfg["V_D"]), I_S=np.float64(cfg["I_S"]), V_sat=np.float64(cfg["V_sat"]))
         print(f"{name} saved")
 
+    # 9. Measured-codebook forward (measured_deployment/operator.py:163-206),
+    #    plain torch on CPU: 24 curves on a non-uniform Vg grid, random
+    #    assignment, inputs partly outside the lookup range; autograd dX.
+    from isa.measured_deployment.operator import DeploymentAwareCIMLinear
+    for name, (m, k, o), g_pts in (("measured_small", (40, 48, 36), 33), ("measured_ragged", (19, 37, 45), 9)):
+        torch.manual_seed(11)
+        layer = DeploymentAwareCIMLinear(k, o)
+        layer.set_r_tia(2.0e4)
+        vg = np.sort(rng.uniform(-0.5, 4.5, g_pts)).astype(np.float32)
+        vg[0], vg[-1] = -0.5, 4.5
+        base = np.exp(rng.uniform(-14, -11, (24, 1))) * np.cumsum(rng.uniform(0.0, 1.0, (24, g_pts)), axis=1)
+        currents = base.astype(np.float32)
+        layer.configure_codebook(torch.from_numpy(vg), torch.from_numpy(currents))
+        pos = rng.integers(0, 24, (o, k)).astype(np.int16)
+        neg = rng.integers(0, 24, (o, k)).astype(np.int16)
+        layer.set_assignment(torch.from_numpy(pos), torch.from_numpy(neg))
+        layer.set_forward_mode("measured")
+        x = rng.uniform(-1.0, 5.0, (1, m, k)).astype(np.float32)
+        xt = torch.from_numpy(x).requires_grad_(True)
+        out = layer(xt)
+        g = rng.standard_normal(out.shape).astype(np.float32)
+        out.backward(torch.from_numpy(g))
+        np.savez_compressed(HERE / f"golden_{name}.npz", x=x[0], vg=vg, currents=currents, pos=pos, neg=neg,
+                            r_tia=np.float64(2.0e4), out=out.detach().numpy()[0], grad_out=g[0],
+                            grad_x=xt.grad.numpy()[0], lookup_min=np.float64(layer.lookup_min),
+                            lookup_max=np.float64(layer.lookup_max))
+        print(f"{name} saved")
+
 
 if __name__ == "__main__":
     main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

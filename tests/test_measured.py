@@ -1,0 +1,79 @@
+"""Measured-codebook deployment path: the fp64 oracle pinned to the reference's
+own CPU code (golden vectors) and its unit test; the sm_100a kernels against both."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import measured as mref
+from tests._util import assert_close_scaled, load_golden
+
+CASES = ["measured_small", "measured_ragged"]
+
+
+def _args(g):
+    return g["vg"], g["currents"], g["pos"], g["neg"], float(g["lookup_min"]), float(g["lookup_max"]), float(g["r_tia"])
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_oracle_matches_reference_measured_forward(case):
+    g = load_golden(case)
+    out, idiff, mag = mref.forward(g["x"], *_args(g))
+    assert_close_scaled(out, g["out"], mag * float(g["r_tia"]), what=f"{case} out")
+    gx, gmag = mref.backward_x(g["x"], *_args(g), g["grad_out"])
+    assert_close_scaled(gx, g["grad_x"], gmag, what=f"{case} grad_x")
+
+
+def test_oracle_reference_unit_case():
+    """The reference's own KAT (tests/test_measured_deployment.py:37-49)."""
+    out, _, _ = mref.forward(np.array([[0.25, 0.5]]), [0.0, 1.0, 2.0], [[0.0, 1.0, 2.0], [0.0, 2.0, 4.0]],
+                             [[1, 1]], [[0, 0]], 0.0, 4.0, 1.0)
+    assert abs(out[0, 0] - 0.75) < 1e-6
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", CASES)
+def test_measured_kernels_match_reference(case):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from isa_b200.operators.measured import DeploymentAwareCIMLinear
+    g = load_golden(case)
+    m, k = g["x"].shape
+    o = g["pos"].shape[0]
+    layer = DeploymentAwareCIMLinear(k, o).cuda()
+    layer.set_r_tia(float(g["r_tia"]))
+    layer.configure_codebook(torch.from_numpy(g["vg"]), torch.from_numpy(g["currents"]))
+    layer.set_assignment(torch.from_numpy(g["pos"]), torch.from_numpy(g["neg"]))
+    layer.set_forward_mode("measured")
+    x = torch.from_numpy(g["x"]).cuda().reshape(1, m, k).requires_grad_(True)
+    out = layer(x)
+    out.backward(torch.from_numpy(g["grad_out"]).cuda().reshape(1, m, o))
+    _, _, mag = mref.forward(g["x"], *_args(g))
+    assert_close_scaled(out.detach().cpu().numpy()[0], g["out"], mag * float(g["r_tia"]), what="out vs reference")
+    _, gmag = mref.backward_x(g["x"], *_args(g), g["grad_out"])
+    assert_close_scaled(x.grad.cpu().numpy()[0], g["grad_x"], gmag, what="grad_x vs reference")
+    assert layer.vth_pos.grad is None  # fixed buffers: no threshold gradient
+
+
+@pytest.mark.gpu
+def test_measured_modes_and_unit_case():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from isa_b200.operators.measured import DeploymentAwareCIMLinear
+    layer = DeploymentAwareCIMLinear(2, 1).cuda()
+    layer.set_r_tia(1.0)
+    layer.configure_codebook(torch.tensor([0.0, 1.0, 2.0]), torch.tensor([[0.0, 1.0, 2.0], [0.0, 2.0, 4.0]]))
+    layer.set_assignment(torch.tensor([[1, 1]], dtype=torch.int16), torch.tensor([[0, 0]], dtype=torch.int16))
+    layer.set_forward_mode("measured")
+    out = layer(torch.tensor([[[0.25, 0.50]]], device="cuda"))
+    assert torch.allclose(out.cpu(), torch.tensor([[[0.75]]]), atol=1e-6)
+    # STE: measured value, continuous (EKV LUT) gradient
+    x = torch.rand(1, 5, 2, device="cuda", requires_grad=True)
+    layer.set_forward_mode("ste")
+    y = layer(x)
+    layer.set_forward_mode("measured")
+    torch.testing.assert_close(y.detach(), layer(x).detach())
+    y.sum().backward()
+    assert layer.vth_pos.grad is not None  # gradient came from the continuous path
+    with pytest.raises(NotImplementedError):
+        layer.configure_codebook(torch.tensor([0.0, 1.0]), torch.tensor([[0.0, 1.0]]), vin_lut_bins=4)
