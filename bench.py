@@ -45,6 +45,9 @@ WORKLOADS = {
     # 256 images x 197 tokens, 384 -> 1536, 24 measured curves on a 33-point Vg grid
     "vit_l_fc1_measured": dict(model="ViT-L fc1, measured 24-state codebook", d=384, hidden=1536, batch=256,
                                seq=197, lut=8192, measured=True),
+    # Physical ViT-L training step, 224x224 images, patch 16 (197 tokens), global batch 256
+    "vit_l_step": dict(model="Physical ViT-L (d=384, 6 heads, 12 layers, hidden 1536, 200 classes)", d=384,
+                       hidden=1536, batch=256, seq=197, lut=8192, layers=12),
     # Physical GPT-L full training step, global batch 64 x 1024 (strong scaling)
     "gpt_l_step": dict(model="Physical GPT-L (d=768, ffn 3072, 12 layers, 12 heads, vocab 50257)", d=768,
                        hidden=3072, batch=64, seq=1024, lut=4096, layers=12),
@@ -480,6 +483,74 @@ def run_reference(args, wl):
     print(json.dumps(rec), flush=True)
 
 
+def run_vit_l(args, wl):
+    """Full Physical ViT-L training step (fp16 autocast + GradScaler, DDP,
+    clip, AdamW, clamp_vth); the global batch is fixed, split across ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from isa_b200.harness.vit import PhysicalViT, ViTConfig, train_step
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    per = wl["batch"] // world
+    torch.manual_seed(0)
+    model = PhysicalViT(ViTConfig()).to(dev)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4)
+    scaler = torch.amp.GradScaler("cuda")
+    cims = model.cim_layers()
+    net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local]) if world > 1 else model
+    gen = torch.Generator(device="cpu").manual_seed(200 + rank)
+    img_host = torch.randn(per, 3, 224, 224, generator=gen).pin_memory()
+    lab_host = torch.randint(0, 200, (per,), generator=gen).pin_memory()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(args.warmup, 3)):
+        train_step(net, opt, scaler, img_host.to(dev), lab_host.to(dev), cims)
+    barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    loss_host = torch.empty((), pin_memory=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        barrier()
+        for s_, e_ in ev:
+            s_.record()
+            loss = train_step(net, opt, scaler, img_host.to(dev, non_blocking=True),
+                              lab_host.to(dev, non_blocking=True), cims)
+            loss_host.copy_(loss, non_blocking=True)
+            e_.record()
+        barrier()
+    t = torch.tensor([sum(s_.elapsed_time(e_) for s_, e_ in ev)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    images = wl["batch"] * args.steps
+    if rank == 0:
+        cells = images * wl["seq"] * wl["layers"] * cells_per_token(wl)
+        rec = {"metric": "Physical ViT-L train images/s", "value": images / (ms * 1e-3), "unit": "images/s",
+               "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+               "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+               "dtype": "f32 CIM / fp16 digital", "data": "synthetic images ~ N(0,1), uniform labels, random init",
+               "config": {"workload": "vit_l_step", "model": wl["model"], "global_batch": wl["batch"],
+                          "tokens_per_image": wl["seq"], "parallelism": f"dp{world}", "lut_size": wl["lut"]},
+               "tokens_per_s": images * wl["seq"] / (ms * 1e-3),
+               "cim_gcell_evals_per_s": cells / (ms * 1e-3) / 1e9,
+               "e2e": {"value": images / (ms * 1e-3), "unit": "images/s",
+                       "h2d_bytes_per_step": img_host.numel() * 4 + lab_host.numel() * 8, "d2h_bytes_per_step": 4},
+               "loss": float(loss_host), "clocks": clocks.summary(), "impl": "ours"}
+        print(json.dumps(rec), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_gpt_l(args, wl):
     """Full Physical GPT-L training step (forward, backward, DDP all-reduce,
     clip, AdamW, clamp_vth); the global batch is fixed, split across ranks."""
@@ -611,6 +682,9 @@ def main():
     wl = WORKLOADS[args.workload]
     if wl.get("measured"):
         run_measured(args, wl)
+        return
+    if args.workload == "vit_l_step":
+        run_vit_l(args, wl)
         return
     if args.workload == "gpt_l_step":
         if args.impl != "ours":
