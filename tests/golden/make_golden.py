@@ -187,6 +187,16 @@ def main(ref_root: str) -> None:
                             V_D=np.float64(cfg["V_D"]), I_S=np.float64(cfg["I_S"]), V_sat=np.float64(cfg["V_sat"]))
         print(f"{name} saved")
 
+    # 8b. State-dict layout of the reference modules (checkpoint compatibility).
+    import json
+    from isa.operators.cim import HybridFFN, PhysicalFFN
+    layout = {}
+    for name, mod in (("CIMLinear", CIMLinear(12, 20)), ("PhysicalFFN", PhysicalFFN(12, 20)),
+                      ("HybridFFN", HybridFFN(12, 20))):
+        layout[name] = {k: [list(v.shape), str(v.dtype)] for k, v in mod.state_dict().items()}
+    (HERE / "reference_state_dict_layout.json").write_text(json.dumps(layout, indent=1, sort_keys=True))
+    print("state-dict layout saved")
+
     # 9. Measured-codebook forward (measured_deployment/operator.py:163-206),
     #    plain torch on CPU: 24 curves on a non-uniform Vg grid, random
     #    assignment, inputs partly outside the lookup range; autograd dX.

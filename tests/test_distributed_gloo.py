@@ -64,3 +64,41 @@ def test_shard_rows_cover_exactly():
         for w in (1, 2, 3, 8):
             idx = np.concatenate([np.arange(n)[shard_rows(n, r, w)] for r in range(w)])
             np.testing.assert_array_equal(idx, np.arange(n))
+
+
+def _failing_worker(rank, world, port, result_path):
+    """Rank 1 dies before the gradient exchange; rank 0 must get an error from
+    its collective within the process-group timeout instead of hanging."""
+    import datetime
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    sys.path[:0] = [str(root), str(root / "isa-_b200")]
+    from isa_b200.distributed import allreduce_gradients
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(0)  # a rank that leaves between steps
+    p = torch.nn.Parameter(torch.zeros(4))
+    p.grad = torch.ones(4)
+    try:
+        allreduce_gradients([p])
+        outcome = "completed"
+    except Exception as exc:  # noqa: BLE001 - any collective error is the detection signal
+        outcome = "error: " + type(exc).__name__
+    Path(result_path).write_text(outcome)
+
+
+def test_lost_rank_is_detected_by_collective_timeout(tmp_path):
+    out = tmp_path / "r.txt"
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, str(out))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    assert out.exists() and out.read_text().startswith("error"), out.read_text() if out.exists() else "no result"
