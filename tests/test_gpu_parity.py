@@ -201,3 +201,41 @@ def test_partial_gradients_and_determinism():
     np.testing.assert_array_equal(only_x[0], full[0])
     np.testing.assert_array_equal(only_w[1], full[1])
     np.testing.assert_array_equal(only_w[2], full[2])
+
+
+def test_nan_inputs_follow_the_oracle():
+    """A NaN input poisons its own row/column sums and nothing else (and the
+    kernels take the clamped path for the tile that holds it)."""
+    tib, tdb, dmin, scale, size = cfg_tables(4096)
+    lut = pack(tib, tdb)
+    rng = np.random.default_rng(5)
+    m, k, o = 70, 20, 40
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    x[3, 7] = np.nan
+    wp = (2.5 + rng.uniform(-0.1, 0.1, (o, k))).astype(np.float32)
+    wn = (2.5 + rng.uniform(-0.1, 0.1, (o, k))).astype(np.float32)
+    wp[5, 2] = np.nan
+    g = rng.standard_normal((m, o)).astype(np.float32)
+    out = gpu_forward(x, wp, wn, lut, dmin, scale, size)
+    ref = oracle.forward(x, wp, wn, bf16_bits_to_f32(tib), dmin, scale, CFG_V_SAT)
+    np.testing.assert_array_equal(np.isnan(out), np.isnan(ref))
+    ok = ~np.isnan(ref)
+    _, mag = oracle.forward(np.nan_to_num(x), np.nan_to_num(wp), wn, bf16_bits_to_f32(tib), dmin, scale,
+                            CFG_V_SAT, with_mag=True)
+    assert_close_scaled(np.where(ok, out, 0), np.where(ok, ref, 0), mag, what="NaN-free outputs")
+    gx, gwp, gwn = gpu_backward(x, wp, wn, g, lut, dmin, scale, size)
+    rx, rwp, rwn = oracle.backward(x, wp, wn, g, bf16_bits_to_f32(tib), bf16_bits_to_f32(tdb), dmin, scale,
+                                   CFG_V_SAT)
+    for a, b in ((gx, rx), (gwp, rwp), (gwn, rwn)):
+        np.testing.assert_array_equal(np.isnan(a), np.isnan(b))
+
+
+@pytest.mark.parametrize("shape", [(1, 384, 1536), (4096, 1, 7), (33, 5, 1)])
+def test_degenerate_shapes_and_largest_table(shape):
+    m, k, o = shape
+    rng = np.random.default_rng(m + 2 * k + 3 * o)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    wp = (2.5 + rng.uniform(-0.1, 0.1, (o, k))).astype(np.float32)
+    wn = (2.5 + rng.uniform(-0.1, 0.1, (o, k))).astype(np.float32)
+    g = rng.standard_normal((m, o)).astype(np.float32)
+    check_all(x, wp, wn, g, *cfg_tables(16384), tag=f"{shape} T=16384")
