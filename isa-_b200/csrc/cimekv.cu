@@ -18,10 +18,15 @@
 //    f inside the table (checked with the same monotone fp32 ops per tile);
 //  * tables are packed as bf16 pairs (the reference tables are bf16-exact,
 //    delta_lut.py:35), so one 32-bit shared load returns both interpolation
-//    nodes of the forward and one 64-bit load the four nodes of the backward;
+//    nodes of I, and one more (same index, fixed offset) both nodes of dI/dV;
+//  * two adjacent tokens share every fp32 instruction through sm_100's packed
+//    f32x2 arithmetic (bit-identical to two scalar ops);
 //  * the backward computes dX and dVth from the same lookups in one pass; dX
 //    is reduced in registers over all outputs, dVth over the tile's tokens in
-//    shared memory and over token splits by a deterministic second kernel.
+//    shared memory and over token splits by a deterministic second kernel;
+//  * the same tiles also run the exact EKV formula instead of the table
+//    (cfg ekv_approx != "lut"), and the forward epilogue can apply the TIA
+//    stage (* R_TIA, signed clamp).
 
 #include <cuda_runtime.h>
 
