@@ -454,6 +454,7 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
     lc.di_s = p.di_s;
     lc.kappa = p.kappa;
     const float r_tia = p.tia_out != nullptr ? __ldg(p.r_tia) : 0.0f;
+    const float inv_vsat = 1.0f / p.vsat;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_m = (p.M + kFwdMT - 1) / kFwdMT;
     const int tiles_o = (p.O + kFwdOT - 1) / kFwdOT;
@@ -495,7 +496,9 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
                 const bool valid = k < p.K && m0 + row < p.M;
                 const float xv = rx[r];
                 xs[kk * kFwdLD + row] = xv;
-                is[kk * kFwdLD + row] = valid ? __frcp_rn(__fadd_rn(1.0f, __fdiv_rn(xv, p.vsat))) : 0.0f;
+                // 1/(1 + x/V_sat) to within 2 ulp (the reference divides; the difference is far
+                // below the fp32 summation error of the K-term sum)
+                is[kk * kFwdLD + row] = valid ? __fdividef(1.0f, fmaf(xv, inv_vsat, 1.0f)) : 0.0f;
                 ps[kk * kFwdLD + row] = rp[r];
                 ns[kk * kFwdLD + row] = rn[r];
                 rng.x = fminf(rng.x, xv);
