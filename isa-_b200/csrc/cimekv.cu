@@ -200,29 +200,48 @@ struct LutConsts {
     f32x2 dmin2, scale2, two23;
     float fmax_;
     uint32_t tab_base;
-    // exact-formula mode: 1/(2 n U_T), V_D, I_S, 2 I_S/(2 n U_T), exp(-V_D/(2 n U_T))
-    float inv, vd, i_s, di_s, kappa;
+    // exact-formula mode: 1/(2 n U_T), V_D, I_S, 2 I_S/(2 n U_T)
+    float inv, vd, i_s, di_s;
 };
 
 // ---- exact EKV branch current (no table) ----
 // I(dV)      = I_S (sp(u1)^2 - sp(u2)^2),  u1 = dV/(2nU_T), u2 = (dV - V_D)/(2nU_T)
 // dI/d(dV)   = I_S 2/(2nU_T) (sp(u1) sig(u1) - sp(u2) sig(u2))
-// with sp(u) = u for u > 20 else log(1 + e^u) (the reference's _softplus,
-// ekv_triton.py:23-25, and torch's softplus threshold), sig = e^u/(1+e^u).
-// e^u2 is taken as e^u1 * exp(-V_D/(2nU_T)).
+// sp = softplus, sig = logistic (the reference's _softplus/_sigmoid,
+// ekv_triton.py:23-31; torch softplus on the CPU path).
+//
+// softplus without a library log: sp(u) = max(u, 0) + log1p(t), t = e^-|u| in
+// (0, 1], and log1p(t) = 2 atanh(z) with z = t / (2 + t) <= 1/3, summed by its
+// odd power series 2 z (1 + z^2/3 + ... + z^12/13); the first omitted term is
+// below 2e-8 relative.  This keeps full relative accuracy deep in subthreshold
+// (where log(1 + e^u) in fp32 rounds to 0).  The same t gives the logistic:
+// sig(u) = 1/(1+t) for u >= 0, t/(1+t) otherwise.
+__device__ __forceinline__ void softplus_sigmoid(float u, float& sp, float* sig) {
+    const float t = __expf(-fabsf(u));
+    const float z = __fdividef(t, 2.0f + t);
+    const float z2 = z * z;
+    float p = 1.0f / 13.0f;
+    p = fmaf(p, z2, 1.0f / 11.0f);
+    p = fmaf(p, z2, 1.0f / 9.0f);
+    p = fmaf(p, z2, 1.0f / 7.0f);
+    p = fmaf(p, z2, 1.0f / 5.0f);
+    p = fmaf(p, z2, 1.0f / 3.0f);
+    p = fmaf(p, z2, 1.0f);
+    sp = fmaxf(u, 0.0f) + 2.0f * z * p;
+    if (sig != nullptr) {
+        const float r = __fdividef(1.0f, 1.0f + t);
+        *sig = u >= 0.0f ? r : t * r;
+    }
+}
+
 __device__ __forceinline__ void ekv_exact1(float dv, const LutConsts& c, float& base, float* deriv) {
     const float u1 = __fmul_rn(dv, c.inv);
     const float u2 = __fmul_rn(__fsub_rn(dv, c.vd), c.inv);
-    const float t1 = __expf(u1);
-    const float t2 = t1 * c.kappa;
-    const float sp1 = u1 > 20.0f ? u1 : log1pf(t1);  // accurate for small t (subthreshold)
-    const float sp2 = u2 > 20.0f ? u2 : log1pf(t2);
+    float sp1, sp2, s1, s2;
+    softplus_sigmoid(u1, sp1, deriv ? &s1 : nullptr);
+    softplus_sigmoid(u2, sp2, deriv ? &s2 : nullptr);
     base = c.i_s * (sp1 * sp1 - sp2 * sp2);
-    if (deriv != nullptr) {
-        const float s1 = u1 > 20.0f ? 1.0f : t1 * __fdividef(1.0f, 1.0f + t1);
-        const float s2 = u2 > 20.0f ? 1.0f : t2 * __fdividef(1.0f, 1.0f + t2);
-        *deriv = c.di_s * (sp1 * s1 - sp2 * s2);
-    }
+    if (deriv != nullptr) *deriv = c.di_s * (sp1 * s1 - sp2 * s2);
 }
 
 __device__ __forceinline__ f32x2 exact_fwd2(f32x2 xx, f32x2 ww, const LutConsts& c) {
@@ -382,7 +401,7 @@ struct FwdParams {
     float* tia_out;           // optional clamp(I_diff * R_TIA, tia_lo, tia_hi)
     int M, K, O, T;
     float dmin, scale, vsat, out_min, out_max, tia_lo, tia_hi;
-    float inv, vd, i_s, di_s, kappa;  // exact-formula mode
+    float inv, vd, i_s, di_s;  // exact-formula mode
 };
 
 // torch.clamp semantics (NaN passes through).
@@ -452,7 +471,6 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
     lc.vd = p.vd;
     lc.i_s = p.i_s;
     lc.di_s = p.di_s;
-    lc.kappa = p.kappa;
     const float r_tia = p.tia_out != nullptr ? __ldg(p.r_tia) : 0.0f;
     const float inv_vsat = 1.0f / p.vsat;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -579,7 +597,7 @@ struct BwdParams {
     int M, K, O, T;
     int tiles_m, nsplit;
     float dmin, scale, vsat;
-    float inv, vd, i_s, di_s, kappa;  // exact-formula mode (kStride == 0)
+    float inv, vd, i_s, di_s;  // exact-formula mode (kStride == 0)
 };
 
 // Table stride (words) of the backward: the smallest supported size >= T.
@@ -714,7 +732,6 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
     lc.vd = p.vd;
     lc.i_s = p.i_s;
     lc.di_s = p.di_s;
-    lc.kappa = p.kappa;
 
     // Threshold range of this CTA's inputs over all outputs (pads count as 0).
     float4 wr;
@@ -999,7 +1016,7 @@ int cimekv_lut_pack(const uint16_t* table_i, const uint16_t* table_ddelta, int t
 }
 
 struct ExactArgs {
-    float inv, vd, i_s, di_s, kappa;
+    float inv, vd, i_s, di_s;
 };
 
 ExactArgs exact_args(float inv_2nut, float v_d, float i_s) {
@@ -1008,7 +1025,6 @@ ExactArgs exact_args(float inv_2nut, float v_d, float i_s) {
     e.vd = v_d;
     e.i_s = i_s;
     e.di_s = (float)(2.0 * (double)inv_2nut * (double)i_s);
-    e.kappa = (float)exp(-(double)v_d * (double)inv_2nut);
     return e;
 }
 
@@ -1057,7 +1073,6 @@ static int launch_forward(const float* x, const float* wpos, const float* wneg, 
     p.vd = ex ? ex->vd : 0.0f;
     p.i_s = ex ? ex->i_s : 0.0f;
     p.di_s = ex ? ex->di_s : 0.0f;
-    p.kappa = ex ? ex->kappa : 0.0f;
     const long ntiles = (long)((M + kFwdMT - 1) / kFwdMT) * ((O + kFwdOT - 1) / kFwdOT);
     int resident = (int)((228 * 1024) / (smem + 1024));
     if (resident > CIMEKV_FWD_MIN_BLOCKS) resident = CIMEKV_FWD_MIN_BLOCKS;
@@ -1401,7 +1416,6 @@ extern "C" int cimekv_exact_backward(const float* x, const float* wpos, const fl
     p.vd = ex.vd;
     p.i_s = ex.i_s;
     p.di_s = ex.di_s;
-    p.kappa = ex.kappa;
     dim3 grid(plan.kblocks, plan.nsplit);
     bwd_kernel<0><<<grid, kBwdThreads, plan.smem, s>>>(p);
     if ((rc = check_launch("bwd_kernel<exact>"))) return rc;
