@@ -118,3 +118,50 @@ def test_cimlinear_module_matches_oracle():
     z.float().sum().backward()
     for p in ffn.parameters():
         assert p.grad is not None and torch.isfinite(p.grad).all()
+
+
+def _config1():
+    """x[256,192] ~ N(0,1) seed 0, CIMLinear(192,768) init, grad ~ N(0,1) seed 3."""
+    from isa_b200.operators.cim import CIMLinear
+    torch.manual_seed(0)
+    x = torch.randn(256, 192)
+    torch.manual_seed(1)
+    lin = CIMLinear(192, 768)
+    torch.manual_seed(3)
+    g = torch.randn(256, 768)
+    return x.numpy(), lin, g.numpy()
+
+
+def test_config1_full_size_against_oracle():
+    x, lin, g = _config1()
+    wp, wn = lin.vth_pos.detach().numpy(), lin.vth_neg.detach().numpy()
+    tib, tdb, dmin, scale, size = cfg_tables(8192)
+    lut = pack(tib, tdb)
+    xd, pd, nd, gd = (torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (x, wp, wn, g))
+    out, gx, gwp, gwn = _run(xd, pd, nd, gd, lut, dmin, scale, size)
+    ti, td = bf16_bits_to_f32(tib), bf16_bits_to_f32(tdb)
+    ref, mag = oracle.forward(x, wp, wn, ti, dmin, scale, CFG_V_SAT, with_mag=True)
+    assert_close_scaled(out.cpu().numpy(), ref, mag, what="config 1 forward")
+    (rx, rwp, rwn), (mx, mwp, mwn) = oracle.backward(x, wp, wn, g, ti, td, dmin, scale, CFG_V_SAT, with_mag=True)
+    assert_close_scaled(gx.cpu().numpy(), rx, mx, what="config 1 grad_x")
+    assert_close_scaled(gwp.cpu().numpy(), rwp, mwp, what="config 1 grad_wpos")
+    assert_close_scaled(gwn.cpu().numpy(), rwn, mwn, what="config 1 grad_wneg")
+
+
+def test_lut_path_tracks_the_exact_device_model():
+    """Physics sanity check: the bf16 LUT path against the exact EKV formula (the
+    reference's CPU path, in fp64) at config 1 — agreement to ~1e-2 of the summed
+    magnitudes, the gap being the bf16 table quantisation."""
+    x, lin, _ = _config1()
+    x = np.clip(x + 2.0, 0.0, 4.0).astype(np.float32)  # voltage-mapped input range
+    wp, wn = lin.vth_pos.detach().numpy(), lin.vth_neg.detach().numpy()
+    tib, tdb, dmin, scale, size = cfg_tables(8192)
+    lut = pack(tib, tdb)
+    out = torch.empty(256, 768, device="cuda")
+    from isa_b200 import _lib
+    xd, pd, nd = (torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (x, wp, wn))
+    _lib.forward(xd, pd, nd, lut, size, dmin, scale, CFG_V_SAT, -4.0, 4.0, out)
+    from oracle.oracle import exact_consts
+    from isa_b200 import FLASH_TRANSISTOR_EKV_CONFIG as cfg
+    exact, mag = oracle.exact_forward(x, wp, wn, *exact_consts(cfg), with_mag=True)
+    assert_close_scaled(out.cpu().numpy(), exact, mag, rtol=2e-2, what="LUT vs exact formula")
