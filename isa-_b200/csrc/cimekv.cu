@@ -598,15 +598,16 @@ struct BwdParams {
     int tiles_m, nsplit;
     float dmin, scale, vsat;
     float inv, vd, i_s, di_s;  // exact-formula mode (kStride == 0)
+    int dw_global;  // 1: accumulate dVth directly in this CTA's workspace slice (shared memory too small)
 };
 
 // Table stride (words) of the backward: the smallest supported size >= T.
 int bwd_stride(int T) { return T <= 4096 ? 4096 : (T <= 8192 ? 8192 : 16384); }
 
-size_t bwd_smem_bytes_stride(int stride, int O) {
+size_t bwd_smem_bytes_stride(int stride, int O, bool dw_global = false) {
     const int opad = (O + 31) / 32 * 32;
     return (size_t)8 * stride                        // I and dI/dV pair tables (none in exact mode)
-           + (size_t)2 * opad * kBwdKT * 4           // dW accumulator
+           + (dw_global ? 0 : (size_t)2 * opad * kBwdKT * 4)  // dW accumulator
            + (size_t)3 * kBwdMT * kBwdKT * 4         // x, 1/d, -1/(vsat d^2): k-major [4][64]
            + (size_t)2 * 32 * 8 * 4                  // double-buffered chunk thresholds
            + (size_t)2 * 8 * 8 * 32 * 4              // double-buffered cross-warp dW exchange
@@ -688,8 +689,8 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
     const int T = p.T;
     const int opad = (p.O + 31) / 32 * 32;
     uint32_t* tab = reinterpret_cast<uint32_t*>(smem);                // [kStride] I pairs, [kStride] dI pairs
-    float* dWs = reinterpret_cast<float*>(smem + 8 * kStride);       // [2][opad][4]
-    float* Xk = dWs + 2 * opad * kBwdKT;  // [4][64] x
+    float* dWs = reinterpret_cast<float*>(smem + 8 * kStride);       // [2][opad][4] unless dw_global
+    float* Xk = dWs + (p.dw_global ? 0 : 2 * opad * kBwdKT);  // [4][64] x
     float* Ik = Xk + kBwdKT * kBwdMT;      // [4][64] 1/d
     float* Nk = Ik + kBwdKT * kBwdMT;      // [4][64] -1/(v_sat d^2)
     float* wsm = Nk + kBwdKT * kBwdMT;     // [2][32 outputs][8]
@@ -719,7 +720,15 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
             tab[i] = p.lut_i[i];
             tab[kStride + i] = p.lut_d[i];
         }
-        for (int i = threadIdx.x; i < 2 * opad * kBwdKT; i += blockDim.x) dWs[i] = 0.0f;
+        if (!p.dw_global) {
+            for (int i = threadIdx.x; i < 2 * opad * kBwdKT; i += blockDim.x) dWs[i] = 0.0f;
+        } else if (p.part != nullptr) {  // this CTA's slice of the workspace is its accumulator
+            for (int e = threadIdx.x; e < 2 * p.O * kBwdKT; e += blockDim.x) {
+                const int br = e / (p.O * kBwdKT), rem = e - br * p.O * kBwdKT;
+                const int o = rem >> 2, kk = rem & 3;
+                if (k0 + kk < p.K) p.part[(((int64_t)split * 2 + br) * p.O + o) * p.K + k0 + kk] = 0.0f;
+            }
+        }
         if (nchunks > 0) wsm[threadIdx.x] = fetch_w(0);  // chunk 0 into buffer 0
     }
     LutConsts lc;
@@ -823,7 +832,12 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
 #pragma unroll
                 for (int w = 0; w < 8; ++w) s += xb[(w * 8 + v) * 32 + lane];
                 const int o = c * 32 + lane;
-                dWs[((v >> 2) * opad + o) * kBwdKT + (v & 3)] += s;
+                if (!p.dw_global) {
+                    dWs[((v >> 2) * opad + o) * kBwdKT + (v & 3)] += s;
+                } else if (p.part != nullptr && o < p.O && k0 + (v & 3) < p.K) {
+                    // only this thread ever touches this element of the CTA's slice
+                    p.part[(((int64_t)split * 2 + (v >> 2)) * p.O + o) * p.K + k0 + (v & 3)] += s;
+                }
             }
             buf ^= 1;
         }
@@ -851,7 +865,7 @@ __global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
         }
     }
     __syncthreads();
-    if (p.part != nullptr) {
+    if (p.part != nullptr && !p.dw_global) {
         for (int e = threadIdx.x; e < 2 * p.O * kBwdKT; e += blockDim.x) {
             const int br = e / (p.O * kBwdKT);
             const int rem = e - br * p.O * kBwdKT;
@@ -933,6 +947,7 @@ __global__ void sum_partials_kernel(const float* __restrict__ partial, int n, fl
 struct BwdPlan {
     int kblocks, tiles_m, nsplit;
     size_t smem, workspace;
+    int dw_global;
 };
 
 // stride: table stride of the kernel instance (0 = exact formula, no table);
@@ -944,7 +959,13 @@ int plan_backward(int M, int K, int O, int T, BwdPlan* plan, int stride = -1) {
     if ((rc = device_limits(dev, &sms, &optin))) return rc;
     plan->kblocks = (K + kBwdKT - 1) / kBwdKT;
     plan->tiles_m = (M + kBwdMT - 1) / kBwdMT;
-    plan->smem = bwd_smem_bytes_stride(stride < 0 ? bwd_stride(T) : stride, O);
+    const int st = stride < 0 ? bwd_stride(T) : stride;
+    plan->smem = bwd_smem_bytes_stride(st, O);
+    plan->dw_global = 0;
+    if (plan->smem > (size_t)optin) {  // large tables with many outputs: dVth accumulator in the workspace
+        plan->smem = bwd_smem_bytes_stride(st, O, true);
+        plan->dw_global = 1;
+    }
     if (plan->smem > (size_t)optin) {
         return set_error(CIMEKV_ELUT_TOO_LARGE,
                          "backward needs %zu B of shared memory (LUT size %d, out_features %d); device allows %d",
@@ -1192,6 +1213,7 @@ int cimekv_backward(const float* x, const float* wpos, const float* wneg, const 
     p.T = table_size;
     p.tiles_m = plan.tiles_m;
     p.nsplit = plan.nsplit;
+    p.dw_global = plan.dw_global;
     p.dmin = delta_min;
     p.scale = delta_scale;
     p.vsat = v_sat;
@@ -1325,6 +1347,7 @@ extern "C" int cimekv_backward_noalloc(const float* x, const float* wpos, const 
     p.T = table_size;
     p.tiles_m = plan.tiles_m;
     p.nsplit = plan.nsplit;
+    p.dw_global = plan.dw_global;
     p.dmin = delta_min;
     p.scale = delta_scale;
     p.vsat = v_sat;
@@ -1409,6 +1432,7 @@ extern "C" int cimekv_exact_backward(const float* x, const float* wpos, const fl
     p.T = 0;
     p.tiles_m = plan.tiles_m;
     p.nsplit = plan.nsplit;
+    p.dw_global = plan.dw_global;
     p.dmin = 0.0f;
     p.scale = 1.0f;
     p.vsat = v_sat;

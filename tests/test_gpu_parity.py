@@ -239,3 +239,16 @@ def test_degenerate_shapes_and_largest_table(shape):
     wn = (2.5 + rng.uniform(-0.1, 0.1, (o, k))).astype(np.float32)
     g = rng.standard_normal((m, o)).astype(np.float32)
     check_all(x, wp, wn, g, *cfg_tables(16384), tag=f"{shape} T=16384")
+
+
+def test_largest_table_with_many_outputs():
+    """T=16384 (the reference default without a cfg size) and 3072 outputs: the
+    backward's dVth accumulator no longer fits shared memory and moves to the
+    workspace."""
+    rng = np.random.default_rng(17)
+    m, k, o = 150, 9, 3072
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    wp = (2.5 + rng.uniform(-0.1, 0.1, (o, k))).astype(np.float32)
+    wn = (2.5 + rng.uniform(-0.1, 0.1, (o, k))).astype(np.float32)
+    g = rng.standard_normal((m, o)).astype(np.float32)
+    check_all(x, wp, wn, g, *cfg_tables(16384), tag="T=16384 O=3072")
