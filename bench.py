@@ -441,7 +441,7 @@ def run_ours(args, wl):
                          "hbm_peak_gbs": measured_peaks().get("hbm_gbs")},
             "cpu_baseline": cpu,
             "clocks": clk,
-            "gpu_launches": 6 * args.steps,
+            "gpu_launches": 10 * args.steps,  # per projection: fwd, tia_bwd, sum_partials, bwd, bwd_reduce
             "impl": "ours",
         }
         print(json.dumps(rec), flush=True)
@@ -619,7 +619,7 @@ def run_gpt_l(args, wl):
                        "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(),
                        "d2h_bytes_per_step": 4},
                "loss": float(loss_host), "clocks": clocks.summary(),
-               "gpu_launches": 6 * 2 * wl["layers"] * args.steps, "impl": "ours"}
+               "gpu_launches": 10 * wl["layers"] * args.steps, "impl": "ours"}
         print(json.dumps(rec), flush=True)
     if world > 1:
         dist.destroy_process_group()
