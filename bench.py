@@ -38,6 +38,9 @@ WORKLOADS = {
     "gpt_m_ffn": dict(model="Physical GPT-M FFN block", d=384, hidden=1536, batch=32, seq=1024, lut=4096),
     # Physical ViT-M FFN block, batch 128 x 65 tokens, T = 8192
     "vit_m_ffn": dict(model="Physical ViT-M FFN block", d=256, hidden=1024, batch=128, seq=65, lut=8192),
+    # Config 3, Hybrid variant: CIM up projection + bf16 digital nn.Linear down projection
+    "gpt_m_ffn_hybrid": dict(model="Hybrid GPT-M FFN block", d=384, hidden=1536, batch=32, seq=1024, lut=4096,
+                             hybrid=True),
     # Config 3 with the exact-formula path (cfg ekv_approx="exact"; the LUT is the default)
     "gpt_m_ffn_exact": dict(model="Physical GPT-M FFN block, exact EKV formula", d=384, hidden=1536, batch=32,
                             seq=1024, lut=4096, approx="exact"),
@@ -73,7 +76,8 @@ def parse():
 
 
 def cells_per_token(wl) -> int:
-    return 2 * wl["d"] * wl["hidden"]
+    """CIM cells per token: both projections (Physical) or the up projection only (Hybrid)."""
+    return (1 if wl.get("hybrid") else 2) * wl["d"] * wl["hidden"]
 
 
 # ------------------------------------------------------------------ clocks --
@@ -189,12 +193,16 @@ def make_ffn(wl, dev, seed=0, reference=False):
         from isa.operators.cim import PhysicalFFN
     else:
         from isa_b200 import make_flash_transistor_ekv_config
-        from isa_b200.operators.cim import PhysicalFFN
+        from isa_b200.operators.cim import HybridFFN, PhysicalFFN
 
     cfg = make_flash_transistor_ekv_config(default_lut_size=wl["lut"])
     cfg["LUT_DELTA_SIZE"] = wl["lut"]
     cfg["ekv_approx"] = wl.get("approx", "lut")
     torch.manual_seed(seed)
+    if wl.get("hybrid"):
+        if reference:
+            from isa.operators.cim import HybridFFN
+        return HybridFFN(wl["d"], wl["hidden"], cfg).to(dev), cfg
     return PhysicalFFN(wl["d"], wl["hidden"], cfg).to(dev), cfg
 
 
@@ -231,7 +239,10 @@ def time_kernels(ffn, cfg, x, dev, reps=5):
         _lib.forward(x1, ffn.fc1.vth_pos, ffn.fc1.vth_neg, lut, geo.size, geo.delta_min_f32, geo.scale,
                      float(cfg["V_sat"]), -4.0, 4.0, h)
         h = (h * ffn.fc1.r_tia).clamp(-4, 4).contiguous()
+        from isa_b200.operators.cim import CIMLinear
         for name, lin, xin in (("fc1", ffn.fc1, x1), ("fc2", ffn.fc2, h)):
+            if not isinstance(lin, CIMLinear):  # Hybrid: digital down projection
+                continue
             m, k = xin.shape
             o = lin.out_features
             out = torch.empty(m, o, device=dev)
