@@ -42,6 +42,9 @@
 #ifndef CIMEKV_FWD_MIN_BLOCKS
 #define CIMEKV_FWD_MIN_BLOCKS 3  // resident forward CTAs per SM the register budget is sized for
 #endif
+#ifndef CIMEKV_BWD_DW_FOR_OCCUPANCY
+#define CIMEKV_BWD_DW_FOR_OCCUPANCY 1  // trade the shared dVth accumulator for a 2nd resident CTA
+#endif
 #ifndef CIMEKV_FWD_KK_UNROLL
 #define CIMEKV_FWD_KK_UNROLL 2
 #endif
@@ -962,8 +965,12 @@ int plan_backward(int M, int K, int O, int T, BwdPlan* plan, int stride = -1) {
     const int st = stride < 0 ? bwd_stride(T) : stride;
     plan->smem = bwd_smem_bytes_stride(st, O);
     plan->dw_global = 0;
-    if (plan->smem > (size_t)optin) {  // large tables with many outputs: dVth accumulator in the workspace
-        plan->smem = bwd_smem_bytes_stride(st, O, true);
+    const size_t per_sm_smem = 228 * 1024;
+    const size_t smem_global = bwd_smem_bytes_stride(st, O, true);
+    if (plan->smem > (size_t)optin ||  // large tables with many outputs, or
+        (CIMEKV_BWD_DW_FOR_OCCUPANCY && 2 * (plan->smem + 1024) > per_sm_smem &&
+         2 * (smem_global + 1024) <= per_sm_smem)) {  // a second resident CTA per SM
+        plan->smem = smem_global;  // dVth accumulator in the workspace
         plan->dw_global = 1;
     }
     if (plan->smem > (size_t)optin) {
