@@ -34,9 +34,9 @@ for _p in (ROOT, ROOT / "isa-_b200"):
         sys.path.insert(0, str(_p))
 
 WORKLOADS = {
-    # Physical GPT-M FFN block, batch 32 x seq 1024, T = 4096
+    # benchmark config 3: Physical GPT-M FFN block, batch 32 x seq 1024, T = 4096
     "gpt_m_ffn": dict(model="Physical GPT-M FFN block", d=384, hidden=1536, batch=32, seq=1024, lut=4096),
-    # Physical ViT-M FFN block, batch 128 x 65 tokens, T = 8192
+    # benchmark config 2: Physical ViT-M FFN block, batch 128 x 65 tokens, T = 8192
     "vit_m_ffn": dict(model="Physical ViT-M FFN block", d=256, hidden=1024, batch=128, seq=65, lut=8192),
     # Config 3, Hybrid variant: CIM up projection + bf16 digital nn.Linear down projection
     "gpt_m_ffn_hybrid": dict(model="Hybrid GPT-M FFN block", d=384, hidden=1536, batch=32, seq=1024, lut=4096,
@@ -48,10 +48,10 @@ WORKLOADS = {
     # 256 images x 197 tokens, 384 -> 1536, 24 measured curves on a 33-point Vg grid
     "vit_l_fc1_measured": dict(model="ViT-L fc1, measured 24-state codebook", d=384, hidden=1536, batch=256,
                                seq=197, lut=8192, measured=True),
-    # Physical ViT-L training step, 224x224 images, patch 16 (197 tokens), global batch 256
+    # benchmark config 5: Physical ViT-L training step, 224x224 images, patch 16 (197 tokens), global batch 256
     "vit_l_step": dict(model="Physical ViT-L (d=384, 6 heads, 12 layers, hidden 1536, 200 classes)", d=384,
                        hidden=1536, batch=256, seq=197, lut=8192, layers=12),
-    # Physical GPT-L full training step, global batch 64 x 1024 (strong scaling)
+    # benchmark config 4: Physical GPT-L full training step, global batch 64 x 1024 (strong scaling)
     "gpt_l_step": dict(model="Physical GPT-L (d=768, ffn 3072, 12 layers, 12 heads, vocab 50257)", d=768,
                        hidden=3072, batch=64, seq=1024, lut=4096, layers=12),
 }
