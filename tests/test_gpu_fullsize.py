@@ -121,7 +121,7 @@ def test_cimlinear_module_matches_oracle():
 
 
 def _config1():
-    """x[256,192] ~ N(0,1) seed 0, CIMLinear(192,768) init, grad ~ N(0,1) seed 3."""
+    """Benchmark config 1: x[256,192] ~ N(0,1) seed 0, CIMLinear(192,768) init, grad ~ N(0,1) seed 3."""
     from isa_b200.operators.cim import CIMLinear
     torch.manual_seed(0)
     x = torch.randn(256, 192)
