@@ -43,6 +43,9 @@
 #ifndef CIMEKV_FWD_MIN_BLOCKS
 #define CIMEKV_FWD_MIN_BLOCKS 3  // resident forward CTAs per SM the register budget is sized for
 #endif
+#ifndef CIMEKV_BWD_MIN_BLOCKS
+#define CIMEKV_BWD_MIN_BLOCKS 2  // resident backward CTAs per SM the register budget is sized for
+#endif
 #ifndef CIMEKV_BWD_DW_FOR_OCCUPANCY
 #define CIMEKV_BWD_DW_FOR_OCCUPANCY 1  // trade the shared dVth accumulator for a 2nd resident CTA
 #endif
@@ -695,7 +698,7 @@ __device__ __forceinline__ void bwd_chunk(const float* __restrict__ Xk, const fl
 }
 
 template <int kStride>
-__global__ void __launch_bounds__(kBwdThreads, 2) bwd_kernel(BwdParams p) {
+__global__ void __launch_bounds__(kBwdThreads, CIMEKV_BWD_MIN_BLOCKS) bwd_kernel(BwdParams p) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int T = p.T;
     const int opad = (p.O + 31) / 32 * 32;
@@ -989,7 +992,7 @@ int plan_backward(int M, int K, int O, int T, BwdPlan* plan, int stride = -1) {
     // Resident CTAs per SM: 2 by registers, fewer if shared memory is short.
     const size_t per_sm = 228 * 1024;
     int resident = (int)(per_sm / (plan->smem + 1024));
-    if (resident > 2) resident = 2;
+    if (resident > CIMEKV_BWD_MIN_BLOCKS) resident = CIMEKV_BWD_MIN_BLOCKS;
     if (resident < 1) resident = 1;
     const int slots = sms * resident;
     int best = 1;
