@@ -215,6 +215,17 @@ int cimekv_backward_noalloc(const float* x, const float* wpos, const float* wneg
                             float* grad_x, float* grad_wpos, float* grad_wneg, void* stream);
 
 /*
+ * Debug support, no counterpart in the reference.  cimekv_debug_build()
+ * returns 1 for the library variant built with CIMEKV_DEBUG_BOUNDS=1
+ * (libcimekv_debug.so), whose kernels check every table index against the
+ * table size and count violations instead of reading out of bounds;
+ * cimekv_debug_oob_count(reset) returns that count (synchronising with the
+ * device; 0 in release builds) and optionally clears it.
+ */
+int cimekv_debug_build(void);
+unsigned int cimekv_debug_oob_count(int reset);
+
+/*
  * Measurement utility with no counterpart in the reference: launches `blocks`
  * CTAs of 256 threads that each issue iters*128 independent FFMAs, and
  * reports the lane-ops issued in *lane_ops.  Timed with events by the caller,

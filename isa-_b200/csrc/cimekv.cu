@@ -43,6 +43,9 @@
 #ifndef CIMEKV_FWD_MIN_BLOCKS
 #define CIMEKV_FWD_MIN_BLOCKS 3  // resident forward CTAs per SM the register budget is sized for
 #endif
+#ifndef CIMEKV_DEBUG_BOUNDS
+#define CIMEKV_DEBUG_BOUNDS 0  // 1: check every table index against T (debug library variant)
+#endif
 #ifndef CIMEKV_BWD_MIN_BLOCKS
 #define CIMEKV_BWD_MIN_BLOCKS 2  // resident backward CTAs per SM the register budget is sized for
 #endif
@@ -133,6 +136,8 @@ int allow_smem(int dev, int slot, Kernel kernel, int smem_optin) {
 
 // ------------------------------------------------------ table + indexing --
 
+__device__ unsigned int g_debug_oob_count = 0;  // table-index violations seen by debug builds
+
 constexpr float kTwo23 = 8388608.0f;       // 2^23
 constexpr uint32_t kTwo23Bits = 0x4B000000u;  // bit pattern of 2^23
 
@@ -214,6 +219,7 @@ struct LutConsts {
     f32x2 dmin2, scale2, two23;
     float fmax_;
     uint32_t tab_base;
+    int T;  // table entries (bounds checks of debug builds)
     // exact-formula mode: 1/(2 n U_T), V_D, I_S, 2 I_S/(2 n U_T)
     float inv, vd, i_s, di_s;
 };
@@ -275,6 +281,17 @@ __device__ __forceinline__ void exact_bwd2(f32x2 xx, f32x2 ww, const LutConsts& 
     deriv = pk2(g0, g1);
 }
 
+#if CIMEKV_DEBUG_BOUNDS
+// Debug builds: a table index outside [0, T) is counted and redirected to entry
+// 0 instead of reading outside the staged table.
+__device__ __forceinline__ void debug_check_index(uint32_t& bits, int T) {
+    if (bits - kTwo23Bits >= (uint32_t)T) {
+        atomicAdd(&g_debug_oob_count, 1u);
+        bits = kTwo23Bits;
+    }
+}
+#endif
+
 // Table coordinate of two lookups (two tokens against one threshold):
 // returns the bit patterns of t = f + 2^23 (rz) per half and a = f - trunc(f).
 template <bool kClamp>
@@ -290,6 +307,10 @@ __device__ __forceinline__ f32x2 lut_coord2(f32x2 xx, f32x2 ww, const LutConsts&
     unpk2(t, t0, t1);
     b0 = __float_as_uint(t0);
     b1 = __float_as_uint(t1);
+#if CIMEKV_DEBUG_BOUNDS
+    debug_check_index(b0, c.T);
+    debug_check_index(b1, c.T);
+#endif
     return sub2(f, sub2(t, c.two23));
 }
 
@@ -478,6 +499,7 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
     LutConsts lc;
     lc.tab_base = smem_u32addr(tab) - (kTwo23Bits << 2);
     lc.fmax_ = static_cast<float>(T - 1);
+    lc.T = T;
     lc.dmin2 = pk2(p.dmin, p.dmin);
     lc.scale2 = pk2(p.scale, p.scale);
     lc.two23 = pk2(kTwo23, kTwo23);
@@ -748,6 +770,7 @@ __global__ void __launch_bounds__(kBwdThreads, CIMEKV_BWD_MIN_BLOCKS) bwd_kernel
     LutConsts lc;
     lc.tab_base = smem_u32addr(tab) - (kTwo23Bits << 2);
     lc.fmax_ = static_cast<float>(T - 1);
+    lc.T = T;
     lc.dmin2 = pk2(p.dmin, p.dmin);
     lc.scale2 = pk2(p.scale, p.scale);
     lc.two23 = pk2(kTwo23, kTwo23);
@@ -1477,3 +1500,17 @@ extern "C" int cimekv_exact_backward(const float* x, const float* wpos, const fl
     }
     return CIMEKV_OK;
 }
+
+// ======================================================== debug support ==
+
+extern "C" unsigned int cimekv_debug_oob_count(int reset) {
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_debug_oob_count, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+    if (reset) {
+        const unsigned int zero = 0;
+        cudaMemcpyToSymbol(g_debug_oob_count, &zero, sizeof(zero));
+    }
+    return v;
+}
+
+extern "C" int cimekv_debug_build(void) { return CIMEKV_DEBUG_BOUNDS; }

@@ -49,6 +49,8 @@ SIGNATURES = {
     "cimekv_measured_backward_x": (_c_int, [_vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                                             _c_float, _c_float, _vp, _c_float, _c_float, _vp, _vp, _vp, _vp]),
     "cimekv_lut_index": (_c_int, [_vp, _c_int, _c_int, _c_float, _c_float, _vp, _vp, _vp]),
+    "cimekv_debug_build": (_c_int, []),
+    "cimekv_debug_oob_count": (ctypes.c_uint, [_c_int]),
     "cimekv_fp32_probe": (_c_int, [_vp, _c_int, _c_int, ctypes.POINTER(ctypes.c_longlong), _vp]),
 }
 
@@ -73,6 +75,18 @@ def load() -> ctypes.CDLL:
                 fn.argtypes = args
             _lib = lib
     return _lib
+
+
+def open_variant(path) -> ctypes.CDLL:
+    """Open another build of the library (e.g. the bounds-checking
+    libcimekv_debug.so) side by side with the default one, with the same
+    prototypes. The wrappers in this module keep using the default library."""
+    lib = ctypes.CDLL(str(path))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
 
 
 def library_path() -> Path:

@@ -20,6 +20,7 @@ REPO_ROOT = PKG_DIR.parent.parent
 INCLUDE_DIR = REPO_ROOT / "include"
 LIB_DIR = PKG_DIR / "_lib"
 LIB_PATH = LIB_DIR / "libcimekv.so"
+DEBUG_LIB_PATH = LIB_DIR / "libcimekv_debug.so"  # table-index bounds checks (CIMEKV_DEBUG_BOUNDS=1)
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -39,24 +40,28 @@ def sources() -> list[Path]:
     return sorted(SRC_DIR.glob("*.cu"))
 
 
-def build_library(force: bool = False, verbose: bool = False) -> Path:
-    """Compile csrc/*.cu into _lib/libcimekv.so (skipped when up to date)."""
+def build_library(force: bool = False, verbose: bool = False, debug: bool = False) -> Path:
+    """Compile csrc/*.cu into _lib/libcimekv.so (or the bounds-checking
+    libcimekv_debug.so with debug=True); skipped when up to date."""
     srcs = sources()
     deps = srcs + sorted(INCLUDE_DIR.glob("*.h")) + sorted(SRC_DIR.glob("*.cuh"))
-    if not force and LIB_PATH.exists():
-        mtime = LIB_PATH.stat().st_mtime
+    out = DEBUG_LIB_PATH if debug else LIB_PATH
+    if not force and out.exists():
+        mtime = out.stat().st_mtime
         if all(p.stat().st_mtime <= mtime for p in deps):
-            return LIB_PATH
+            return out
     LIB_DIR.mkdir(parents=True, exist_ok=True)
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = out.with_suffix(".so.tmp")
     cmd = [_nvcc(), *NVCC_FLAGS, f"-I{INCLUDE_DIR}", f"-I{SRC_DIR}", *map(str, srcs), "-o", str(tmp)]
+    if debug:
+        cmd.insert(1, "-DCIMEKV_DEBUG_BOUNDS=1")
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, out)
+    return out
 
 
 if __name__ == "__main__":
-    print(build_library(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_library(force="--force" in sys.argv, verbose="-v" in sys.argv, debug="--debug" in sys.argv))

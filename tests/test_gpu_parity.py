@@ -38,7 +38,8 @@ def pack(table_i_bits, table_dd_bits):
 def gpu_forward(x, wp, wn, lut, dmin, scale, size, v_sat=CFG_V_SAT, out_min=-4.0, out_max=4.0):
     from isa_b200 import _lib
     xd, pd, nd = _dev(x), _dev(wp), _dev(wn)
-    out = torch.empty((x.shape[0], wp.shape[0]), dtype=torch.float32, device="cuda")
+    # NaN canary: an output element the kernel fails to write stays NaN and fails the check
+    out = torch.full((x.shape[0], wp.shape[0]), float("nan"), dtype=torch.float32, device="cuda")
     _lib.forward(xd, pd, nd, lut, size, dmin, scale, v_sat, out_min, out_max, out)
     return out.cpu().numpy()
 
