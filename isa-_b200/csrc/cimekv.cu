@@ -52,6 +52,9 @@
 #ifndef CIMEKV_BWD_DW_FOR_OCCUPANCY
 #define CIMEKV_BWD_DW_FOR_OCCUPANCY 1  // trade the shared dVth accumulator for a 2nd resident CTA
 #endif
+#ifndef CIMEKV_MIXED_BF16
+#define CIMEKV_MIXED_BF16 1  // table differences by mixed bf16/fp32 subtract (sm_100)
+#endif
 #ifndef CIMEKV_FWD_KK_UNROLL
 #define CIMEKV_FWD_KK_UNROLL 2
 #endif
@@ -148,8 +151,28 @@ constexpr uint32_t kTwo23Bits = 0x4B000000u;  // bit pattern of 2^23
 __host__ __device__ inline size_t fwd_table_bytes(int T) { return ((size_t)T * 4 + 15) & ~(size_t)15; }
 
 
-__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+// Low bf16 of a pair word as fp32 (a byte permute, which issues on the ALU
+// pipe and leaves the FMA pipe to the interpolation arithmetic).
+__device__ __forceinline__ float bf16_lo(uint32_t w) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, 0, 0x1044;" : "=r"(r) : "r"(w));
+    return __uint_as_float(r);
+}
+#if !CIMEKV_MIXED_BF16
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+#endif
+
+// hi(w) - lo in one sm_100 mixed-precision subtract (bf16 minus fp32, rounded
+// to fp32): the same value as bf16_hi(w) - lo, since bf16 -> fp32 is exact.
+__device__ __forceinline__ float bf16_hi_minus(uint32_t w, float lo) {
+#if CIMEKV_MIXED_BF16
+    float d;
+    asm("{ .reg .b16 l, h; mov.b32 {l, h}, %1; sub.rn.f32.bf16 %0, h, %2; }" : "=f"(d) : "r"(w), "f"(lo));
+    return d;
+#else
+    return __fsub_rn(bf16_hi(w), lo);
+#endif
+}
 
 // Table coordinate of one lookup: f = (fl(x - w) - dmin) * scale, each step
 // rounded to fp32 (never contracted), optionally clamped to [0, T-1].
@@ -292,6 +315,18 @@ __device__ __forceinline__ void debug_check_index(uint32_t& bits, int T) {
 }
 #endif
 
+// Interpolation of two pair words {v[j], v[j+1]} at fractions a (two tokens):
+// v[j] + a (v[j+1] - v[j]) per half.
+__device__ __forceinline__ f32x2 lerp_pair2(f32x2 a, uint32_t e0, uint32_t e1) {
+    const float l0 = bf16_lo(e0), l1 = bf16_lo(e1);
+#if CIMEKV_MIXED_BF16
+    return fma2(a, pk2(bf16_hi_minus(e0, l0), bf16_hi_minus(e1, l1)), pk2(l0, l1));
+#else
+    const f32x2 q0 = pk2(l0, l1);
+    return fma2(a, sub2(pk2(bf16_hi(e0), bf16_hi(e1)), q0), q0);
+#endif
+}
+
 // Table coordinate of two lookups (two tokens against one threshold):
 // returns the bit patterns of t = f + 2^23 (rz) per half and a = f - trunc(f).
 template <bool kClamp>
@@ -321,9 +356,7 @@ __device__ __forceinline__ f32x2 lut_fwd2(f32x2 xx, f32x2 ww, const LutConsts& c
     const f32x2 a = lut_coord2<kClamp>(xx, ww, c, b0, b1);
     const uint32_t e0 = lds32(c.tab_base + (b0 << 2));
     const uint32_t e1 = lds32(c.tab_base + (b1 << 2));
-    const f32x2 q0 = pk2(bf16_lo(e0), bf16_lo(e1));
-    const f32x2 q1 = pk2(bf16_hi(e0), bf16_hi(e1));
-    return fma2(a, sub2(q1, q0), q0);
+    return lerp_pair2(a, e0, e1);
 }
 
 // fp32 tile-range test: true when every cell of a tile whose x lie in
@@ -665,12 +698,8 @@ __device__ __forceinline__ void lut_bwd2(f32x2 xx, f32x2 ww, const LutConsts& c,
     const uint32_t a0 = c.tab_base + (b0 << 2), a1 = c.tab_base + (b1 << 2);
     const uint32_t i0 = lds32(a0), i1 = lds32(a1);
     const uint32_t d0 = lds32_off<4 * kStride>(a0), d1 = lds32_off<4 * kStride>(a1);
-    const f32x2 qb0 = pk2(bf16_lo(i0), bf16_lo(i1));
-    const f32x2 qb1 = pk2(bf16_hi(i0), bf16_hi(i1));
-    const f32x2 qd0 = pk2(bf16_lo(d0), bf16_lo(d1));
-    const f32x2 qd1 = pk2(bf16_hi(d0), bf16_hi(d1));
-    base = fma2(a, sub2(qb1, qb0), qb0);
-    deriv = fma2(a, sub2(qd1, qd0), qd0);
+    base = lerp_pair2(a, i0, i1);
+    deriv = lerp_pair2(a, d0, d1);
 }
 
 // One chunk of 32 outputs for this thread's 8 tokens (4 pairs) x 4 inputs.
@@ -826,12 +855,19 @@ __global__ void __launch_bounds__(kBwdThreads, CIMEKV_BWD_MIN_BLOCKS) bwd_kernel
         // Register prefetch of g (8 tokens of this warp, output of this lane).
         float gn[kBwdTok];
         auto load_g = [&](int c) {
-            const int o = c * 32 + lane;
-            const bool oin = o < p.O;
+            if (m0 + kBwdMT <= p.M && (c + 1) * 32 <= p.O) {
+                // interior chunk: no bounds tests, one base pointer
+                const float* src = p.g + (int64_t)(m0 + warp * kBwdTok) * p.O + c * 32 + lane;
 #pragma unroll
-            for (int i = 0; i < kBwdTok; ++i) {
-                const int m = m0 + warp * kBwdTok + i;
-                gn[i] = (oin && m < p.M) ? __ldg(p.g + (int64_t)m * p.O + o) : 0.0f;
+                for (int i = 0; i < kBwdTok; ++i) gn[i] = __ldg(src + (int64_t)i * p.O);
+            } else {
+                const int o = c * 32 + lane;
+                const bool oin = o < p.O;
+#pragma unroll
+                for (int i = 0; i < kBwdTok; ++i) {
+                    const int m = m0 + warp * kBwdTok + i;
+                    gn[i] = (oin && m < p.M) ? __ldg(p.g + (int64_t)m * p.O + o) : 0.0f;
+                }
             }
         };
         if (nchunks > 0) load_g(0);
