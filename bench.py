@@ -302,6 +302,31 @@ def cpu_sample(wl, tokens, nthreads=0, seed=0):
     return tokens * cells_per_token(wl), time.perf_counter() - t0
 
 
+def reference_pytorch_cpu(wl, tokens=64, seed=0) -> dict:
+    """The reference's own PyTorch CPU path (its CIMLinear CPU branch: the exact
+    EKV formula, then autograd), fwd+bwd of the unmodified reference block from
+    baseline/_ref on `tokens` tokens with all host threads.  Informational: it
+    evaluates the exact formula, not the LUT, so it is not the parity oracle."""
+    import torch
+
+    if not (ROOT / "baseline" / "_ref" / "isa").exists():
+        return {"unavailable": "baseline/_ref (the pip-installed reference) is not present"}
+    ffn, _ = make_ffn(wl, "cpu", seed=seed, reference=True)
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(1, tokens, wl["d"], generator=gen)
+    g = torch.randn(1, tokens, wl["d"], generator=gen)
+    xw = torch.randn(1, min(tokens, 16), wl["d"], generator=gen)
+    ffn(xw).backward(torch.ones_like(xw))  # warm-up
+    ffn.zero_grad(set_to_none=True)
+    t0 = time.perf_counter()
+    ffn(x).backward(g)
+    sec = time.perf_counter() - t0
+    cells = tokens * cells_per_token(wl)
+    return {"value": cells / sec / 1e9, "unit": "Gcell-evals/s", "cores": torch.get_num_threads(),
+            "kind": "reference", "sample": f"{tokens} tokens, one fwd+bwd of the reference block on CPU, "
+                                           f"{sec:.1f} s", "formula": "exact EKV (the reference's CPU branch)"}
+
+
 # ------------------------------------------------------------ our arm -----
 
 def run_ours(args, wl):
@@ -386,6 +411,9 @@ def run_ours(args, wl):
         cpu = {"value": c / sec / 1e9, "unit": "Gcell-evals/s", "cores": oracle.max_threads(), "kind": "port",
                "sample": f"{args.cpu_sample_tokens} tokens of the block (both projections, fwd+bwd), "
                          f"oracle/cimekv_oracle.c with OpenMP, {sec:.1f} s"}
+    cpu_ref = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not refgpu:
+        cpu_ref = reference_pytorch_cpu(wl)
     if world > 1:
         dist.barrier()
     if rank == 0 and (refgpu or exact):
@@ -397,7 +425,7 @@ def run_ours(args, wl):
                "tokens_per_s": world * tokens * args.steps / (ms_total * 1e-3),
                "step_frac_of_fp32_peak": value / world * (OPS_FWD + OPS_BWD) / peak["sustained"],
                "e2e": {"value": e2e_value / 1e9, "unit": "Gcell-evals/s"},
-               "clocks": clocks.summary(),
+               "clocks": clocks.summary(), "cpu_reference_pytorch": cpu_ref,
                "note": ("unmodified reference package from baseline/_ref through its module API, same workload "
                         "and timing" if refgpu else "exact-formula kernels of this build")}
         print(json.dumps(rec), flush=True)
@@ -451,6 +479,7 @@ def run_ours(args, wl):
                          "ops_per_cell": {"fwd": OPS_FWD, "bwd": OPS_BWD},
                          "hbm_peak_gbs": measured_peaks().get("hbm_gbs")},
             "cpu_baseline": cpu,
+            "cpu_reference_pytorch": cpu_ref,
             "clocks": clk,
             "gpu_launches": 10 * args.steps,  # per projection: fwd, tia_bwd, sum_partials, bwd, bwd_reduce
             "impl": "ours",
@@ -490,6 +519,7 @@ def run_reference(args, wl):
                          "sample": f"{tokens} tokens of the block per step (both projections, fwd+bwd): "
                                    "CPU restatement of the reference LUT path, oracle/cimekv_oracle.c, OpenMP"},
         "e2e": {"value": v, "unit": "Gcell-evals/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_reference_pytorch": reference_pytorch_cpu(wl),
     }
     print(json.dumps(rec), flush=True)
 
