@@ -56,7 +56,7 @@
 #define CIMEKV_MIXED_BF16 1  // table differences by mixed bf16/fp32 subtract (sm_100)
 #endif
 #ifndef CIMEKV_FWD_KK_UNROLL
-#define CIMEKV_FWD_KK_UNROLL 2
+#define CIMEKV_FWD_KK_UNROLL 4
 #endif
 
 namespace {
@@ -482,7 +482,8 @@ __device__ __forceinline__ void fwd_chunk(const float* __restrict__ xs, const fl
                                           const float* __restrict__ ps, const float* __restrict__ ns,
                                           const LutConsts& c, f32x2 (&acc)[4][2]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll kFwdKkUnroll
+    constexpr int kUnroll = kExact ? 2 : kFwdKkUnroll;  // the exact-formula cell is long: less unrolling
+#pragma unroll kUnroll
     for (int kk = 0; kk < kFwdKC; ++kk) {
         const float4 xa = *reinterpret_cast<const float4*>(xs + kk * kFwdLD + warp * 8);
         const float4 xb = *reinterpret_cast<const float4*>(xs + kk * kFwdLD + warp * 8 + 4);
