@@ -454,7 +454,10 @@ constexpr int kFwdKkUnroll = CIMEKV_FWD_KK_UNROLL;
 constexpr int kFwdThreads = 256;
 constexpr int kFwdMT = 64;
 constexpr int kFwdOT = 64;
-constexpr int kFwdKC = 16;
+#ifndef CIMEKV_FWD_KC
+#define CIMEKV_FWD_KC 16  // k-chunk staged per barrier
+#endif
+constexpr int kFwdKC = CIMEKV_FWD_KC;
 constexpr int kFwdLD = 68;  // padded row stride (floats) of the k-major tiles
 constexpr int kFwdStageFloats = 4 * kFwdKC * kFwdLD;
 constexpr int kFwdPerThread = kFwdMT * kFwdKC / kFwdThreads;  // 4 elements of each tile
@@ -563,7 +566,7 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
 #pragma unroll
             for (int r = 0; r < kFwdPerThread; ++r) {
                 const int e = threadIdx.x + kFwdThreads * r;
-                const int row = e >> 4, k = k0 + (e & 15);
+                const int row = e / kFwdKC, k = k0 + (e % kFwdKC);
                 const bool kin = k < p.K;
                 const int gm = m0 + row, go = o0 + row;
                 rx[r] = (kin && gm < p.M) ? __ldg(p.x + (int64_t)gm * p.K + k) : 0.0f;
@@ -579,7 +582,7 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
 #pragma unroll
             for (int r = 0; r < kFwdPerThread; ++r) {
                 const int e = threadIdx.x + kFwdThreads * r;
-                const int row = e >> 4, kk = e & 15;
+                const int row = e / kFwdKC, kk = e % kFwdKC;
                 const int k = c * kFwdKC + kk;
                 const bool valid = k < p.K && m0 + row < p.M;
                 const float xv = rx[r];
