@@ -165,6 +165,9 @@ int cimekv_measured_forward(const float* x, const int16_t* pos_idx, const int16_
  * there is no threshold gradient; r_tia is detached as in the reference):
  *   grad_x[m,k] = [lookup_min <= x <= lookup_max]
  *                 * sum_o g[m,o] r [out_min <= idiff r <= out_max] (a_p - a_n)[j(x)]
+ * The slopes (4 S (G-1) bytes) and the assignment of 4 inputs (16 O bytes)
+ * are held in shared memory: CIMEKV_ELUT_TOO_LARGE when they exceed it
+ * (O up to about 10000 with the largest codebook).
  */
 int cimekv_measured_backward_x(const float* x, const int16_t* pos_idx, const int16_t* neg_idx,
                                const float* vg, const float* coef, int M, int K, int O, int S, int G,

@@ -33,6 +33,10 @@ int fail(int code, const char* msg) {
     return code;
 }
 
+#ifndef CIMEKV_MEAS_FWD_CTAS
+#define CIMEKV_MEAS_FWD_CTAS 4  // resident forward CTAs per SM (persistent grid)
+#endif
+
 constexpr int kThreads = 256;
 constexpr int kMT = 64;   // tokens per tile
 constexpr int kOT = 64;   // outputs per tile
@@ -69,23 +73,51 @@ __device__ __forceinline__ int segment_of(const float* vg, int G, float v) {
 
 __device__ __forceinline__ float clamp_nan(float v, float lo, float hi) { return v < lo ? lo : (v > hi ? hi : v); }
 
-__global__ void __launch_bounds__(kThreads) measured_fwd_kernel(MeasParams p) {
-    extern __shared__ __align__(16) unsigned char smem[];
+// The codebook in shared memory: slopes and intercepts as two tables laid out
+// [segment][state], the intercepts at a compile-time byte offset kIcOff from
+// the slopes (one address serves both loads).  A warp's lanes (outputs) read
+// one segment at their states, i.e. at most S <= 32 adjacent words of one
+// table: conflict-free.
+template <int kIcOff>
+__device__ __forceinline__ void stage_codebook(const MeasParams& p, float* sl, float* vg, bool with_icpt) {
     const int nseg = p.G - 1;
-    // Coefficients transposed to [segment][state]: a warp reads one segment for
-    // its lanes' (random) states, i.e. adjacent words instead of a fixed stride.
-    float2* coef = reinterpret_cast<float2*>(smem);                  // [G-1][S]
-    float* vg = reinterpret_cast<float*>(coef + p.S * nseg);         // [G] (+pad)
-    float* xs = vg + ((p.G + 3) & ~3);                                // [KC][LD] clamped x
-    int* js = reinterpret_cast<int*>(xs + kKC * kLD);                 // [KC][LD] segment * S
-    int* ps = js + kKC * kLD;                                         // [KC][LD] pos state
-    int* ns = ps + kKC * kLD;                                         // [KC][LD] neg state
     for (int i = threadIdx.x; i < p.S * nseg; i += blockDim.x) {
         const int st = i / nseg, sg = i - st * nseg;
-        coef[sg * p.S + st] = p.coef[i];
+        const float2 c = p.coef[i];
+        sl[sg * p.S + st] = c.x;
+        if (with_icpt) sl[kIcOff / 4 + sg * p.S + st] = c.y;
     }
     for (int i = threadIdx.x; i < p.G; i += blockDim.x) vg[i] = p.vg[i];
+}
+
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+    float v;
+    asm("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+template <int kOff>
+__device__ __forceinline__ float lds_f32_off(uint32_t addr) {
+    float v;
+    asm("ld.shared.f32 %0, [%1+%2];" : "=f"(v) : "r"(addr), "n"(kOff));
+    return v;
+}
+
+// Byte size of the slope + intercept region of the forward (kIcOff each).
+constexpr int kIcOffSmall = 4096;   // S*(G-1) <= 1024
+constexpr int kIcOffLarge = 65536;  // S*(G-1) <= 16384
+
+template <int kIcOff>
+__global__ void __launch_bounds__(kThreads) measured_fwd_kernel(MeasParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    float* sl = reinterpret_cast<float*>(smem);                       // [G-1][S] slopes; intercepts at +kIcOff
+    float* vg = reinterpret_cast<float*>(smem + 2 * kIcOff);           // [G] (+pad)
+    float* xs = vg + ((p.G + 3) & ~3);                                // [KC][LD] clamped x
+    int* js = reinterpret_cast<int*>(xs + kKC * kLD);                 // [KC][LD] byte offset of the segment row
+    int* ps = js + kKC * kLD;                                         // [KC][LD] pos state * 4
+    int* ns = ps + kKC * kLD;                                         // [KC][LD] neg state * 4
+    stage_codebook<kIcOff>(p, sl, vg, true);
     __syncthreads();
+    const uint32_t sl_base = static_cast<uint32_t>(__cvta_generic_to_shared(sl));
     const float r = __ldg(p.r_tia);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_o = (p.O + kOT - 1) / kOT;
@@ -105,13 +137,14 @@ __global__ void __launch_bounds__(kThreads) measured_fwd_kernel(MeasParams p) {
                 xv = fminf(fmaxf(xv, p.lookup_min), p.lookup_max);  // torch clamp on a finite range
                 // (padded k beyond K is staged but never summed: the loop below stops at kc)
                 xs[kk * kLD + row] = xv;
-                js[kk * kLD + row] = segment_of(vg, p.G, xv) * p.S;
+                js[kk * kLD + row] = (int)sl_base + segment_of(vg, p.G, xv) * p.S * 4;
                 const bool oin = kin && o < p.O;
-                ps[kk * kLD + row] = oin ? (int)p.pos[(int64_t)o * p.K + k] : 0;
-                ns[kk * kLD + row] = oin ? (int)p.neg[(int64_t)o * p.K + k] : 0;
+                ps[kk * kLD + row] = oin ? (int)p.pos[(int64_t)o * p.K + k] * 4 : 0;
+                ns[kk * kLD + row] = oin ? (int)p.neg[(int64_t)o * p.K + k] * 4 : 0;
             }
             __syncthreads();
             const int kc = p.K - k0 < kKC ? p.K - k0 : kKC;
+#pragma unroll 2
             for (int kk = 0; kk < kc; ++kk) {
                 int pi[2], ni[2];
 #pragma unroll
@@ -119,14 +152,20 @@ __global__ void __launch_bounds__(kThreads) measured_fwd_kernel(MeasParams p) {
                     pi[j] = ps[kk * kLD + lane + 32 * j];
                     ni[j] = ns[kk * kLD + lane + 32 * j];
                 }
+                const float4 xa = *reinterpret_cast<const float4*>(xs + kk * kLD + warp * 8);
+                const float4 xb = *reinterpret_cast<const float4*>(xs + kk * kLD + warp * 8 + 4);
+                const int4 ja = *reinterpret_cast<const int4*>(js + kk * kLD + warp * 8);
+                const int4 jb = *reinterpret_cast<const int4*>(js + kk * kLD + warp * 8 + 4);
+                const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+                const int seg[8] = {ja.x, ja.y, ja.z, ja.w, jb.x, jb.y, jb.z, jb.w};
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const float xv = xs[kk * kLD + warp * 8 + i];
-                    const int seg = js[kk * kLD + warp * 8 + i];
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
-                        const float2 cp = coef[pi[j] + seg], cn = coef[ni[j] + seg];
-                        acc[i][j] += fmaf(xv, cp.x - cn.x, cp.y - cn.y);
+                        const uint32_t ap = (uint32_t)(seg[i] + pi[j]), an = (uint32_t)(seg[i] + ni[j]);
+                        const float da = lds_f32(ap) - lds_f32(an);
+                        const float db = lds_f32_off<kIcOff>(ap) - lds_f32_off<kIcOff>(an);
+                        acc[i][j] += fmaf(xv[i], da, db);
                     }
                 }
             }
@@ -148,41 +187,132 @@ __global__ void __launch_bounds__(kThreads) measured_fwd_kernel(MeasParams p) {
 
 // grad_x[m,k] = [lookup_min <= x <= lookup_max] * sum_o g'[m,o] (a_p - a_n)[seg(x)]
 // with g' = g * r_tia * [lo <= idiff * r_tia <= hi] (the autograd of the
-// reference's clamp(x), masked GEMMs, * r_tia and clamp).  One thread per
-// (m,k); the warp shares m, so g' is a broadcast read.
-__global__ void __launch_bounds__(kThreads) measured_dx_kernel(MeasParams p, const float* __restrict__ g,
-                                                                float* __restrict__ gx) {
+// reference's clamp(x), masked GEMMs, * r_tia and clamp).
+//
+// Tiled like the forward: CTA = kDxKT inputs x one token split; per 64-token
+// tile, warp w owns tokens [8w, 8w+8) and lane l walks outputs o = 32c + l, so
+// the slope gathers of a warp hit one segment row at the lanes' states
+// (conflict-free).  g' is formed once per (token, output) per CTA from
+// loads prefetched a chunk ahead; the assignment of the CTA's inputs
+// ([O][kDxKT] pos/neg) is staged once.  dX of a thread's 8 tokens x 4 inputs
+// sums in registers over its outputs, then one 32-lane transpose-reduce per
+// tile.
+constexpr int kDxKT = 4;
+constexpr int kDxMinBlocks = 3;
+
+__global__ void __launch_bounds__(kThreads, kDxMinBlocks)
+    measured_dx_kernel(MeasParams p, const float* __restrict__ g, float* __restrict__ gx, int nsplit) {
     extern __shared__ __align__(16) unsigned char smem[];
-    const int nseg = p.G - 1;
-    float2* coef = reinterpret_cast<float2*>(smem);  // [G-1][S]
-    float* vg = reinterpret_cast<float*>(coef + p.S * nseg);
-    for (int i = threadIdx.x; i < p.S * nseg; i += blockDim.x) {
-        const int st = i / nseg, sg = i - st * nseg;
-        coef[sg * p.S + st] = p.coef[i];
+    const int ncoef = p.S * (p.G - 1);
+    const int opad = (p.O + 31) / 32 * 32;
+    float* sl = reinterpret_cast<float*>(smem);                       // [G-1][S] slopes
+    float* vg = sl + ((ncoef + 3) & ~3);                               // [G] (+pad to 16 bytes)
+    int* seg_s = reinterpret_cast<int*>(vg + ((p.G + 3) & ~3));        // [4 inputs][64 tokens] row address
+    int* ok_s = seg_s + kMT * kDxKT;                                   // [4 inputs][64 tokens] x inside the range
+    int4* st_s = reinterpret_cast<int4*>(ok_s + kMT * kDxKT);          // [opad] {4p | 4n << 16} per input
+    stage_codebook<0>(p, sl, vg, false);
+    const uint32_t sl_base = static_cast<uint32_t>(__cvta_generic_to_shared(sl));
+    const int k0 = blockIdx.x * kDxKT;
+    for (int o = threadIdx.x; o < opad; o += blockDim.x) {
+        int v[kDxKT];
+#pragma unroll
+        for (int kk = 0; kk < kDxKT; ++kk) {
+            const int k = k0 + kk;
+            const bool in = o < p.O && k < p.K;
+            const int ps = in ? (int)p.pos[(int64_t)o * p.K + k] : 0;
+            const int ns = in ? (int)p.neg[(int64_t)o * p.K + k] : 0;
+            v[kk] = (int)((uint32_t)(ps * 4) | ((uint32_t)(ns * 4) << 16));
+        }
+        st_s[o] = make_int4(v[0], v[1], v[2], v[3]);
     }
-    for (int i = threadIdx.x; i < p.G; i += blockDim.x) vg[i] = p.vg[i];
-    __syncthreads();
     const float r = __ldg(p.r_tia);
-    const int64_t n = (int64_t)p.M * p.K;
-    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t m = e / p.K;
-        const int k = (int)(e - m * p.K);
-        const float xr = p.x[e];
-        if (!(xr >= p.lookup_min && xr <= p.lookup_max)) {  // clamp passes no gradient
-            gx[e] = 0.0f;
-            continue;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_m = (p.M + kMT - 1) / kMT;
+    const int tile_lo = (int)((int64_t)blockIdx.y * tiles_m / nsplit);
+    const int tile_hi = (int)((int64_t)(blockIdx.y + 1) * tiles_m / nsplit);
+    const int nchunks = opad / 32;
+    for (int tile = tile_lo; tile < tile_hi; ++tile) {
+        const int m0 = tile * kMT;
+        __syncthreads();  // codebook/assignment staged; previous tile's readers of seg_s done
+        {
+            const int t = threadIdx.x >> 2, kk = threadIdx.x & 3;
+            const int m = m0 + t, k = k0 + kk;
+            int sg = 0, ok = 0;
+            if (m < p.M && k < p.K) {
+                const float xr = __ldg(p.x + (int64_t)m * p.K + k);
+                if (xr >= p.lookup_min && xr <= p.lookup_max) {
+                    sg = segment_of(vg, p.G, xr) * p.S * 4;
+                    ok = 1;
+                }
+            }
+            seg_s[kk * kMT + t] = (int)sl_base + sg;
+            ok_s[kk * kMT + t] = ok;
         }
-        const int seg = segment_of(vg, p.G, xr) * p.S;
-        float acc = 0.0f;
-        for (int o = 0; o < p.O; ++o) {
-            const float id = p.idiff[m * p.O + o];
-            const float v = __fmul_rn(id, r);
-            if (!(v >= p.lo && v <= p.hi)) continue;
-            const float gm = __fmul_rn(g[m * p.O + o], r);
-            const int64_t w = (int64_t)o * p.K + k;
-            acc = fmaf(gm, coef[seg + (int)p.pos[w]].x - coef[seg + (int)p.neg[w]].x, acc);
+        __syncthreads();
+        // Upstream gradient and I_diff of this warp's 8 tokens at output
+        // 32c + lane, prefetched one chunk ahead (both loads in flight at once).
+        float nid[8], ng[8];
+        const bool rows_full = m0 + kMT <= p.M;
+        auto load = [&](int c) {
+            const int o = c * 32 + lane;
+            const int64_t e0 = (int64_t)(m0 + warp * 8) * p.O + o;
+            if (rows_full && (c + 1) * 32 <= p.O) {  // interior chunk: no bounds tests
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    nid[i] = __ldg(p.idiff + e0 + (int64_t)i * p.O);
+                    ng[i] = __ldg(g + e0 + (int64_t)i * p.O);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const bool in = o < p.O && m0 + warp * 8 + i < p.M;
+                    nid[i] = in ? __ldg(p.idiff + e0 + (int64_t)i * p.O) : 0.0f;
+                    ng[i] = in ? __ldg(g + e0 + (int64_t)i * p.O) : 0.0f;
+                }
+            }
+        };
+        float dx[8 * kDxKT];
+#pragma unroll
+        for (int i = 0; i < 8 * kDxKT; ++i) dx[i] = 0.0f;
+        if (nchunks > 0) load(0);
+        for (int c = 0; c < nchunks; ++c) {
+            float gm[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float v = __fmul_rn(nid[i], r);
+                gm[i] = (v >= p.lo && v <= p.hi) ? __fmul_rn(ng[i], r) : 0.0f;
+            }
+            if (c + 1 < nchunks) load(c + 1);
+            const int4 st = st_s[c * 32 + lane];
+            const int sv[kDxKT] = {st.x, st.y, st.z, st.w};
+#pragma unroll
+            for (int kk = 0; kk < kDxKT; ++kk) {
+                const int pb = sv[kk] & 0xFFFF, nb = (int)((uint32_t)sv[kk] >> 16);
+                const int4 sa = reinterpret_cast<const int4*>(seg_s + kk * kMT + warp * 8)[0];
+                const int4 sb = reinterpret_cast<const int4*>(seg_s + kk * kMT + warp * 8)[1];
+                const int sg[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float da = lds_f32((uint32_t)(sg[i] + pb)) - lds_f32((uint32_t)(sg[i] + nb));
+                    dx[i * kDxKT + kk] = fmaf(gm[i], da, dx[i * kDxKT + kk]);
+                }
+            }
         }
-        gx[e] = acc;
+        // 32-lane transpose-reduce: afterwards lane l holds the sum of element
+        // l = (token l/4, input l%4).
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) {
+            const bool upper = (lane & s) != 0;
+#pragma unroll
+            for (int j = 0; j < s; ++j) {
+                const float send = upper ? dx[j] : dx[j + s];
+                const float keep = upper ? dx[j + s] : dx[j];
+                dx[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+            }
+        }
+        const int t = warp * 8 + (lane >> 2), kk = lane & 3;
+        const int m = m0 + t, k = k0 + kk;
+        if (m < p.M && k < p.K) gx[(int64_t)m * p.K + k] = ok_s[kk * kMT + t] ? dx[0] : 0.0f;
     }
 }
 
@@ -197,10 +327,14 @@ int check_args(const MeasParams& p) {
     return CIMEKV_OK;
 }
 
+int fwd_ic_off(const MeasParams& p) { return (int64_t)p.S * (p.G - 1) * 4 <= kIcOffSmall ? kIcOffSmall : kIcOffLarge; }
+
 size_t smem_bytes(const MeasParams& p, bool fwd) {
-    size_t b = (size_t)p.S * (p.G - 1) * sizeof(float2) + (size_t)((p.G + 3) & ~3) * 4;
-    if (fwd) b += (size_t)4 * kKC * kLD * 4;
-    return b;
+    const size_t ncoef = (size_t)p.S * (p.G - 1);
+    const size_t vgb = (size_t)((p.G + 3) & ~3) * 4;
+    if (fwd) return (size_t)2 * fwd_ic_off(p) + vgb + (size_t)4 * kKC * kLD * 4;
+    return ((ncoef + 3) & ~(size_t)3) * 4 + vgb + (size_t)2 * kMT * kDxKT * 4 +
+           (size_t)(p.O + 31) / 32 * 32 * sizeof(int4);
 }
 
 int launch_setup(const MeasParams& p, bool fwd, size_t* smem, int* sms) {
@@ -210,9 +344,15 @@ int launch_setup(const MeasParams& p, bool fwd, size_t* smem, int* sms) {
     cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     *smem = smem_bytes(p, fwd);
-    if (*smem > (size_t)optin) return fail(CIMEKV_ELUT_TOO_LARGE, "codebook does not fit shared memory");
-    cudaError_t e = fwd ? cudaFuncSetAttribute(measured_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin)
-                        : cudaFuncSetAttribute(measured_dx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+    if (*smem > (size_t)optin)
+        return fail(CIMEKV_ELUT_TOO_LARGE, fwd ? "codebook does not fit shared memory"
+                                               : "codebook plus the [O][4] assignment tile does not fit shared memory");
+    cudaError_t e = !fwd ? cudaFuncSetAttribute(measured_dx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin)
+                    : fwd_ic_off(p) == kIcOffSmall
+                        ? cudaFuncSetAttribute(measured_fwd_kernel<kIcOffSmall>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, optin)
+                        : cudaFuncSetAttribute(measured_fwd_kernel<kIcOffLarge>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
     if (e != cudaSuccess) return fail(CIMEKV_ECUDA, cudaGetErrorString(e));
     return CIMEKV_OK;
 }
@@ -256,9 +396,12 @@ extern "C" int cimekv_measured_forward(const float* x, const int16_t* pos_idx, c
     int sms;
     if ((rc = launch_setup(p, true, &smem, &sms))) return rc;
     const long tiles = (long)((M + kMT - 1) / kMT) * ((O + kOT - 1) / kOT);
-    long grid = (long)sms * 2;
+    long grid = (long)sms * CIMEKV_MEAS_FWD_CTAS;
     if (grid > tiles) grid = tiles;
-    measured_fwd_kernel<<<(unsigned)grid, kThreads, smem, (cudaStream_t)stream>>>(p);
+    if (fwd_ic_off(p) == kIcOffSmall)
+        measured_fwd_kernel<kIcOffSmall><<<(unsigned)grid, kThreads, smem, (cudaStream_t)stream>>>(p);
+    else
+        measured_fwd_kernel<kIcOffLarge><<<(unsigned)grid, kThreads, smem, (cudaStream_t)stream>>>(p);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CIMEKV_OK : fail(CIMEKV_ECUDA, cudaGetErrorString(e));
 }
@@ -277,10 +420,15 @@ extern "C" int cimekv_measured_backward_x(const float* x, const int16_t* pos_idx
     size_t smem;
     int sms;
     if ((rc = launch_setup(p, false, &smem, &sms))) return rc;
-    const int64_t n = (int64_t)M * K;
-    long grid = (long)((n + kThreads - 1) / kThreads);
-    if (grid > (long)sms * 8) grid = (long)sms * 8;
-    measured_dx_kernel<<<(unsigned)grid, kThreads, smem, (cudaStream_t)stream>>>(p, grad_out, grad_x);
+    // grid: one CTA column per group of 4 inputs, the token tiles split into
+    // enough rows for about eight waves of resident CTAs
+    const int kgroups = (K + kDxKT - 1) / kDxKT;
+    const int tiles_m = (M + kMT - 1) / kMT;
+    int nsplit = (8 * kDxMinBlocks * sms + kgroups - 1) / kgroups;  // ~8 waves: small tail
+    if (nsplit > tiles_m) nsplit = tiles_m;
+    if (nsplit < 1) nsplit = 1;
+    measured_dx_kernel<<<dim3((unsigned)kgroups, (unsigned)nsplit), kThreads, smem, (cudaStream_t)stream>>>(
+        p, grad_out, grad_x, nsplit);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CIMEKV_OK : fail(CIMEKV_ECUDA, cudaGetErrorString(e));
 }

@@ -77,3 +77,43 @@ def test_measured_modes_and_unit_case():
     assert layer.vth_pos.grad is not None  # gradient came from the continuous path
     with pytest.raises(NotImplementedError):
         layer.configure_codebook(torch.tensor([0.0, 1.0]), torch.tensor([[0.0, 1.0]]), vin_lut_bins=4)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape,states,grid", [((300, 70, 130), 24, 33), ((1025, 37, 96), 5, 4),
+                                               ((64, 4, 32), 24, 9), ((129, 130, 1), 7, 17), ((7, 3, 65), 1, 2)])
+def test_measured_kernels_random_shapes(shape, states, grid):
+    """Ragged tiles, inputs outside the lookup range, clamped outputs and small
+    codebooks (state tables not a multiple of 4 entries), against the fp64 oracle."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from isa_b200.operators.measured import DeploymentAwareCIMLinear
+    m, k, o = shape
+    rng = np.random.default_rng(m * 7 + k)
+    vg = np.sort(rng.uniform(0.0, 4.0, grid)).astype(np.float32)
+    vg[0], vg[-1] = 0.0, 4.0
+    currents = np.cumsum(rng.uniform(0.0, 2e-6, (states, grid)), axis=1).astype(np.float32)
+    pos = rng.integers(0, states, (o, k)).astype(np.int16)
+    neg = rng.integers(0, states, (o, k)).astype(np.int16)
+    x = rng.uniform(-0.5, 4.5, (m, k)).astype(np.float32)  # some inputs outside [0, 4]
+    layer = DeploymentAwareCIMLinear(k, o).cuda()
+    layer.configure_codebook(torch.from_numpy(vg), torch.from_numpy(currents))
+    layer.set_assignment(torch.from_numpy(pos), torch.from_numpy(neg))
+    layer.set_forward_mode("measured")
+    lmin, lmax = layer.lookup_min, layer.lookup_max
+    # R_TIA so that roughly a third of the outputs hit the clamp
+    _, idiff_ref, _ = mref.forward(x, vg, currents, pos, neg, lmin, lmax, 1.0)
+    r = float(4.0 / max(np.quantile(np.abs(idiff_ref), 0.7), 1e-12))
+    # keep every |idiff * r| away from the clamp edge, where the fp32 kernel and
+    # the fp64 oracle could disagree on the gradient mask
+    while np.min(np.abs(np.abs(idiff_ref * r) - 4.0)) < 1e-3:
+        r *= 1.0007
+    layer.set_r_tia(r)
+    g = rng.standard_normal((m, o)).astype(np.float32)
+    xd = torch.from_numpy(x).cuda().reshape(1, m, k).requires_grad_(True)
+    out = layer(xd)
+    out.backward(torch.from_numpy(g).cuda().reshape(1, m, o))
+    want, _, mag = mref.forward(x, vg, currents, pos, neg, lmin, lmax, r)
+    assert_close_scaled(out.detach().cpu().numpy()[0], want, mag * r, what="measured out")
+    gx_want, gmag = mref.backward_x(x, vg, currents, pos, neg, lmin, lmax, r, g)
+    assert_close_scaled(xd.grad.cpu().numpy()[0], gx_want, gmag, what="measured grad_x")
