@@ -243,8 +243,8 @@ struct LutConsts {
     float fmax_;
     uint32_t tab_base;
     int T;  // table entries (bounds checks of debug builds)
-    // exact-formula mode: 1/(2 n U_T), V_D, I_S, 2 I_S/(2 n U_T)
-    float inv, vd, i_s, di_s;
+    // exact-formula mode: 1/(2 n U_T), V_D
+    float inv, vd;
 };
 
 // ---- exact EKV branch current (no table) ----
@@ -283,8 +283,10 @@ __device__ __forceinline__ void ekv_exact1(float dv, const LutConsts& c, float& 
     float sp1, sp2, s1, s2;
     softplus_sigmoid(u1, sp1, deriv ? &s1 : nullptr);
     softplus_sigmoid(u2, sp2, deriv ? &s2 : nullptr);
-    base = c.i_s * (sp1 * sp1 - sp2 * sp2);
-    if (deriv != nullptr) *deriv = c.di_s * (sp1 * s1 - sp2 * s2);
+    // I/I_S and (dI/dV)/(2 I_S/(2nU_T)): the constant factors are folded into the
+    // per-(token, input) weights the kernels stage (1/d, 1/(V_sat d^2)).
+    base = sp1 * sp1 - sp2 * sp2;
+    if (deriv != nullptr) *deriv = sp1 * s1 - sp2 * s2;
 }
 
 __device__ __forceinline__ f32x2 exact_fwd2(f32x2 xx, f32x2 ww, const LutConsts& c) {
@@ -542,8 +544,6 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
     lc.two23 = pk2(kTwo23, kTwo23);
     lc.inv = p.inv;
     lc.vd = p.vd;
-    lc.i_s = p.i_s;
-    lc.di_s = p.di_s;
     const float r_tia = p.tia_out != nullptr ? __ldg(p.r_tia) : 0.0f;
     const float inv_vsat = 1.0f / p.vsat;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -589,7 +589,8 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
                 xs[kk * kFwdLD + row] = xv;
                 // 1/(1 + x/V_sat) to within 2 ulp (the reference divides; the difference is far
                 // below the fp32 summation error of the K-term sum)
-                is[kk * kFwdLD + row] = valid ? __fdividef(1.0f, fmaf(xv, inv_vsat, 1.0f)) : 0.0f;
+                // (exact mode: times I_S, the factor the cell evaluation leaves out)
+                is[kk * kFwdLD + row] = valid ? __fdividef(kExact ? p.i_s : 1.0f, fmaf(xv, inv_vsat, 1.0f)) : 0.0f;
                 ps[kk * kFwdLD + row] = rp[r];
                 ns[kk * kFwdLD + row] = rn[r];
                 rng.x = fminf(rng.x, xv);
@@ -809,8 +810,6 @@ __global__ void __launch_bounds__(kBwdThreads, CIMEKV_BWD_MIN_BLOCKS) bwd_kernel
     lc.two23 = pk2(kTwo23, kTwo23);
     lc.inv = p.inv;
     lc.vd = p.vd;
-    lc.i_s = p.i_s;
-    lc.di_s = p.di_s;
 
     // Threshold range of this CTA's inputs over all outputs (pads count as 0).
     float4 wr;
@@ -842,8 +841,11 @@ __global__ void __launch_bounds__(kBwdThreads, CIMEKV_BWD_MIN_BLOCKS) bwd_kernel
             xval = valid ? __ldg(p.x + (int64_t)m * p.K + k) : 0.0f;
             const float d = __fadd_rn(1.0f, __fdiv_rn(xval, p.vsat));
             Xk[kk * kBwdMT + t] = xval;
-            Ik[kk * kBwdMT + t] = valid ? __fdiv_rn(1.0f, d) : 0.0f;
-            Nk[kk * kBwdMT + t] = valid ? -__fdiv_rn(1.0f, __fmul_rn(__fmul_rn(p.vsat, d), d)) : 0.0f;
+            // exact mode (kStride == 0): times the constant factors of dI/dV and I
+            // that the cell evaluation leaves out
+            const float fi = kStride == 0 ? p.di_s : 1.0f, fn = kStride == 0 ? p.i_s : 1.0f;
+            Ik[kk * kBwdMT + t] = valid ? __fdiv_rn(fi, d) : 0.0f;
+            Nk[kk * kBwdMT + t] = valid ? -__fdiv_rn(fn, __fmul_rn(__fmul_rn(p.vsat, d), d)) : 0.0f;
         }
         float4 xr;
         bool xnan;
