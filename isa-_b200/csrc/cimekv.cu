@@ -658,6 +658,11 @@ constexpr int kBwdThreads = 256;
 constexpr int kBwdMT = 64;
 constexpr int kBwdKT = 4;
 constexpr int kBwdTok = 8;  // tokens per thread
+// Row stride (floats) of the staged chunk thresholds [32 outputs][8 slots]: 12
+// puts the 128-bit reads of 8 consecutive lanes on 32 distinct banks.
+constexpr int kWsLd = 12;
+// Where thread t's threshold fetch (output t/8, slot t%8) lands in a buffer.
+__device__ __forceinline__ int ws_slot() { return (threadIdx.x >> 3) * kWsLd + (threadIdx.x & 7); }
 
 struct BwdParams {
     const float* x;
@@ -683,7 +688,7 @@ size_t bwd_smem_bytes_stride(int stride, int O, bool dw_global = false) {
     return (size_t)8 * stride                        // I and dI/dV pair tables (none in exact mode)
            + (dw_global ? 0 : (size_t)2 * opad * kBwdKT * 4)  // dW accumulator
            + (size_t)3 * kBwdMT * kBwdKT * 4         // x, 1/d, -1/(vsat d^2): k-major [4][64]
-           + (size_t)2 * 32 * 8 * 4                  // double-buffered chunk thresholds
+           + (size_t)2 * 32 * kWsLd * 4              // double-buffered chunk thresholds
            + (size_t)2 * 8 * 8 * 32 * 4              // double-buffered cross-warp dW exchange
            + 8 * sizeof(float4) + 8 * sizeof(int);   // range reduction
 }
@@ -717,8 +722,8 @@ __device__ __forceinline__ void bwd_chunk(const float* __restrict__ Xk, const fl
                                           f32x2 (&dx)[4][kBwdKT], f32x2 (&ap)[kBwdKT], f32x2 (&an)[kBwdKT]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const f32x2 G[4] = {pk2(g[0], g[1]), pk2(g[2], g[3]), pk2(g[4], g[5]), pk2(g[6], g[7])};
-    const float4 wp4 = *reinterpret_cast<const float4*>(ws + lane * 8);
-    const float4 wn4 = *reinterpret_cast<const float4*>(ws + lane * 8 + 4);
+    const float4 wp4 = *reinterpret_cast<const float4*>(ws + lane * kWsLd);
+    const float4 wn4 = *reinterpret_cast<const float4*>(ws + lane * kWsLd + 4);
     const float wp[4] = {wp4.x, wp4.y, wp4.z, wp4.w};
     const float wn[4] = {wn4.x, wn4.y, wn4.z, wn4.w};
 #pragma unroll
@@ -763,8 +768,8 @@ __global__ void __launch_bounds__(kBwdThreads, CIMEKV_BWD_MIN_BLOCKS) bwd_kernel
     float* Xk = dWs + (p.dw_global ? 0 : 2 * opad * kBwdKT);  // [4][64] x
     float* Ik = Xk + kBwdKT * kBwdMT;      // [4][64] 1/d
     float* Nk = Ik + kBwdKT * kBwdMT;      // [4][64] -1/(v_sat d^2)
-    float* wsm = Nk + kBwdKT * kBwdMT;     // [2][32 outputs][8]
-    float* xch = wsm + 2 * 32 * 8;         // [2][8 warps][8 vals][32 lanes]
+    float* wsm = Nk + kBwdKT * kBwdMT;     // [2][32 outputs][kWsLd]
+    float* xch = wsm + 2 * 32 * kWsLd;     // [2][8 warps][8 vals][32 lanes]
     float4* red = reinterpret_cast<float4*>(xch + 2 * 8 * 8 * 32);
     int* red_nan = reinterpret_cast<int*>(red + 8);
 
@@ -799,7 +804,7 @@ __global__ void __launch_bounds__(kBwdThreads, CIMEKV_BWD_MIN_BLOCKS) bwd_kernel
                 if (k0 + kk < p.K) p.part[(((int64_t)split * 2 + br) * p.O + o) * p.K + k0 + kk] = 0.0f;
             }
         }
-        if (nchunks > 0) wsm[threadIdx.x] = fetch_w(0);  // chunk 0 into buffer 0
+        if (nchunks > 0) wsm[ws_slot()] = fetch_w(0);  // chunk 0 into buffer 0
     }
     LutConsts lc;
     lc.tab_base = smem_u32addr(tab) - (kTwo23Bits << 2);
@@ -884,7 +889,7 @@ __global__ void __launch_bounds__(kBwdThreads, CIMEKV_BWD_MIN_BLOCKS) bwd_kernel
             if (c + 1 < nchunks) load_g(c + 1);
             // next chunk's thresholds (wrapping to chunk 0 for the next tile)
             const float wnext = fetch_w(c + 1 < nchunks ? c + 1 : 0);
-            const float* ws = wsm + buf * (32 * 8);
+            const float* ws = wsm + buf * (32 * kWsLd);
             f32x2 ap2[kBwdKT], an2[kBwdKT];
 #pragma unroll
             for (int kk = 0; kk < kBwdKT; ++kk) ap2[kk] = an2[kk] = pk2(0.0f, 0.0f);
@@ -893,7 +898,7 @@ __global__ void __launch_bounds__(kBwdThreads, CIMEKV_BWD_MIN_BLOCKS) bwd_kernel
             } else {
                 bwd_chunk<true, kStride>(Xk, Ik, Nk, ws, g, lc, dx2, ap2, an2);
             }
-            wsm[(buf ^ 1) * (32 * 8) + threadIdx.x] = wnext;
+            wsm[(buf ^ 1) * (32 * kWsLd) + ws_slot()] = wnext;
             // Cross-warp sum of the dVth partials, accumulated into dWs.
             float* xb = xch + buf * (8 * 8 * 32);
 #pragma unroll
