@@ -13,8 +13,8 @@
 //
 // The segment depends only on (m,k), so it is found once per staged element
 // (binary search over vg in shared memory) and shared by all outputs; the
-// per-cell work is two gathers of {a, b} from a shared-memory coefficient
-// table and two FMAs.
+// per-cell work is four conflict-free 32-bit gathers (slope and intercept of
+// both branches) from shared-memory tables and an FMA.
 
 #include <cuda_runtime.h>
 
@@ -113,8 +113,7 @@ __global__ void __launch_bounds__(kThreads) measured_fwd_kernel(MeasParams p) {
     float* vg = reinterpret_cast<float*>(smem + 2 * kIcOff);           // [G] (+pad)
     float* xs = vg + ((p.G + 3) & ~3);                                // [KC][LD] clamped x
     int* js = reinterpret_cast<int*>(xs + kKC * kLD);                 // [KC][LD] byte offset of the segment row
-    int* ps = js + kKC * kLD;                                         // [KC][LD] pos state * 4
-    int* ns = ps + kKC * kLD;                                         // [KC][LD] neg state * 4
+    uint32_t* ps = reinterpret_cast<uint32_t*>(js + kKC * kLD);       // [KC][LD] 4 pos | 4 neg << 16
     stage_codebook<kIcOff>(p, sl, vg, true);
     __syncthreads();
     const uint32_t sl_base = static_cast<uint32_t>(__cvta_generic_to_shared(sl));
@@ -139,8 +138,9 @@ __global__ void __launch_bounds__(kThreads) measured_fwd_kernel(MeasParams p) {
                 xs[kk * kLD + row] = xv;
                 js[kk * kLD + row] = (int)sl_base + segment_of(vg, p.G, xv) * p.S * 4;
                 const bool oin = kin && o < p.O;
-                ps[kk * kLD + row] = oin ? (int)p.pos[(int64_t)o * p.K + k] * 4 : 0;
-                ns[kk * kLD + row] = oin ? (int)p.neg[(int64_t)o * p.K + k] * 4 : 0;
+                const uint32_t sp = oin ? (uint32_t)p.pos[(int64_t)o * p.K + k] * 4u : 0u;
+                const uint32_t sn = oin ? (uint32_t)p.neg[(int64_t)o * p.K + k] * 4u : 0u;
+                ps[kk * kLD + row] = sp | (sn << 16);
             }
             __syncthreads();
             const int kc = p.K - k0 < kKC ? p.K - k0 : kKC;
@@ -149,8 +149,9 @@ __global__ void __launch_bounds__(kThreads) measured_fwd_kernel(MeasParams p) {
                 int pi[2], ni[2];
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
-                    pi[j] = ps[kk * kLD + lane + 32 * j];
-                    ni[j] = ns[kk * kLD + lane + 32 * j];
+                    const uint32_t v = ps[kk * kLD + lane + 32 * j];
+                    pi[j] = (int)(v & 0xFFFFu);
+                    ni[j] = (int)(v >> 16);
                 }
                 const float4 xa = *reinterpret_cast<const float4*>(xs + kk * kLD + warp * 8);
                 const float4 xb = *reinterpret_cast<const float4*>(xs + kk * kLD + warp * 8 + 4);
@@ -332,7 +333,7 @@ int fwd_ic_off(const MeasParams& p) { return (int64_t)p.S * (p.G - 1) * 4 <= kIc
 size_t smem_bytes(const MeasParams& p, bool fwd) {
     const size_t ncoef = (size_t)p.S * (p.G - 1);
     const size_t vgb = (size_t)((p.G + 3) & ~3) * 4;
-    if (fwd) return (size_t)2 * fwd_ic_off(p) + vgb + (size_t)4 * kKC * kLD * 4;
+    if (fwd) return (size_t)2 * fwd_ic_off(p) + vgb + (size_t)3 * kKC * kLD * 4;
     return ((ncoef + 3) & ~(size_t)3) * 4 + vgb + (size_t)2 * kMT * kDxKT * 4 +
            (size_t)(p.O + 31) / 32 * 32 * sizeof(int4);
 }
