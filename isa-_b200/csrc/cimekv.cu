@@ -243,7 +243,7 @@ struct LutConsts {
     float fmax_;
     uint32_t tab_base;
     int T;  // table entries (bounds checks of debug builds)
-    // exact-formula mode: 1/(2 n U_T), V_D
+    // exact-formula mode: log2(e)/(2 n U_T), V_D log2(e)/(2 n U_T)
     float inv, vd;
 };
 
@@ -253,23 +253,30 @@ struct LutConsts {
 // sp = softplus, sig = logistic (the reference's _softplus/_sigmoid,
 // ekv_triton.py:23-31; torch softplus on the CPU path).
 //
-// softplus without a library log: sp(u) = max(u, 0) + log1p(t), t = e^-|u| in
-// (0, 1], and log1p(t) = 2 atanh(z) with z = t / (2 + t) <= 1/3, evaluated as
-// 2 z P(z^2) with P a degree-4 fit of atanh(z)/z (relative error 4e-9).  This keeps full relative accuracy deep in subthreshold
-// (where log(1 + e^u) in fp32 rounds to 0).  The same t gives the logistic:
-// sig(u) = 1/(1+t) for u >= 0, t/(1+t) otherwise.
+// The kernels work in base-2 units: u' = u log2(e) (so e^-|u| = 2^-|u'|, one
+// SFU op) and sp' = sp log2(e) = max(u', 0) + log2(e) log1p(t); the factors
+// ln2^2 (for I) and ln2 (for dI/dV) ride on the staged per-(token, input)
+// weights with I_S.  log1p(t) = 2 atanh(z), z = t / (2 + t) <= 1/3, with
+// atanh(z)/z a degree-4 polynomial in z^2 fitted for minimum maximum relative
+// error (iteratively reweighted least squares; 4e-9 in exact arithmetic),
+// its coefficients scaled by 2 log2(e).  This keeps full relative accuracy deep
+// in subthreshold (where log(1 + e^u) in fp32 rounds to 0).  The same t gives
+// the logistic: sig(u) = 1/(1+t) for u >= 0, t/(1+t) otherwise.
+__device__ __forceinline__ float exp2_approx(float v) {  // PTX ex2.approx.ftz.f32
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+    return r;
+}
+
 __device__ __forceinline__ void softplus_sigmoid(float u, float& sp, float* sig) {
-    const float t = __expf(-fabsf(u));
+    const float t = exp2_approx(-fabsf(u));
     const float z = __fdividef(t, 2.0f + t);
     const float z2 = z * z;
-    // 2 atanh(z)/z on z^2 in [0, 1/9]: degree-4 polynomial in z^2 fitted for
-    // minimum maximum relative error (iteratively reweighted least squares),
-    // 4e-9 in exact arithmetic (coefficients of atanh(z)/z doubled exactly).
-    float p = 0.28178334f;
-    p = fmaf(p, z2, 0.27960598f);
-    p = fmaf(p, z2, 0.40024912f);
-    p = fmaf(p, z2, 0.66666317f);
-    p = fmaf(p, z2, 2.0f);
+    float p = 0.4065274f;
+    p = fmaf(p, z2, 0.40338615f);
+    p = fmaf(p, z2, 0.5774374f);
+    p = fmaf(p, z2, 0.96179163f);
+    p = fmaf(p, z2, 2.88539004f);
     sp = fmaf(z, p, fmaxf(u, 0.0f));
     if (sig != nullptr) {
         const float r = __fdividef(1.0f, 1.0f + t);
@@ -277,14 +284,15 @@ __device__ __forceinline__ void softplus_sigmoid(float u, float& sp, float* sig)
     }
 }
 
+// c.inv = log2(e)/(2nU_T), c.vd = V_D log2(e)/(2nU_T).
 __device__ __forceinline__ void ekv_exact1(float dv, const LutConsts& c, float& base, float* deriv) {
     const float u1 = __fmul_rn(dv, c.inv);
-    const float u2 = __fmul_rn(__fsub_rn(dv, c.vd), c.inv);
+    const float u2 = __fsub_rn(u1, c.vd);
     float sp1, sp2, s1, s2;
     softplus_sigmoid(u1, sp1, deriv ? &s1 : nullptr);
     softplus_sigmoid(u2, sp2, deriv ? &s2 : nullptr);
-    // I/I_S and (dI/dV)/(2 I_S/(2nU_T)): the constant factors are folded into the
-    // per-(token, input) weights the kernels stage (1/d, 1/(V_sat d^2)).
+    // I/(I_S ln2^2) and (dI/dV)/(2 I_S ln2/(2nU_T)): the constant factors are
+    // folded into the per-(token, input) weights the kernels stage.
     base = sp1 * sp1 - sp2 * sp2;
     if (deriv != nullptr) *deriv = sp1 * s1 - sp2 * s2;
 }
@@ -1129,12 +1137,14 @@ struct ExactArgs {
     float inv, vd, i_s, di_s;
 };
 
+// Constants of the base-2 cell evaluation (see softplus_sigmoid).
 ExactArgs exact_args(float inv_2nut, float v_d, float i_s) {
+    const double log2e = 1.4426950408889634, ln2 = 0.6931471805599453;
     ExactArgs e;
-    e.inv = inv_2nut;
-    e.vd = v_d;
-    e.i_s = i_s;
-    e.di_s = (float)(2.0 * (double)inv_2nut * (double)i_s);
+    e.inv = (float)((double)inv_2nut * log2e);
+    e.vd = (float)((double)v_d * (double)inv_2nut * log2e);
+    e.i_s = (float)((double)i_s * ln2 * ln2);
+    e.di_s = (float)(2.0 * (double)inv_2nut * (double)i_s * ln2);
     return e;
 }
 
