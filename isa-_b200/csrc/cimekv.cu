@@ -495,7 +495,10 @@ __device__ __forceinline__ void fwd_chunk(const float* __restrict__ xs, const fl
                                           const float* __restrict__ ps, const float* __restrict__ ns,
                                           const LutConsts& c, f32x2 (&acc)[4][2]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    constexpr int kUnroll = kExact ? 2 : kFwdKkUnroll;  // the exact-formula cell is long: less unrolling
+#ifndef CIMEKV_FWD_KK_UNROLL_EXACT
+#define CIMEKV_FWD_KK_UNROLL_EXACT 1
+#endif
+    constexpr int kUnroll = kExact ? CIMEKV_FWD_KK_UNROLL_EXACT : kFwdKkUnroll;  // the exact-formula cell is long: less unrolling
 #pragma unroll kUnroll
     for (int kk = 0; kk < kFwdKC; ++kk) {
         const float4 xa = *reinterpret_cast<const float4*>(xs + kk * kFwdLD + warp * 8);
