@@ -62,3 +62,14 @@ def test_operator_refuses_cpu_tensors():
     w = torch.full((3, 8), 2.5)
     with pytest.raises(RuntimeError, match="CUDA"):
         cuda_lut_ekv_matmul(x, w, w, cfg)
+
+
+def test_debug_variant_exports_the_same_symbols():
+    """The bounds-checking build (CIMEKV_DEBUG_BOUNDS=1) is a drop-in for the
+    release library and says which one it is."""
+    from isa_b200 import _lib, build
+    dbg = _lib.open_variant(build.build_library(debug=True))
+    for name in declared_symbols():
+        assert hasattr(dbg, name), name
+    assert dbg.cimekv_debug_build() == 1
+    assert _lib.load().cimekv_debug_build() == 0
