@@ -439,11 +439,16 @@ def run_ours(args, wl):
         dom_ms, dom_name, dom_ops = max(per)
         pk = peak["sustained"]
         achieved = dom_ops / (dom_ms * 1e-3)
-        traffic = None
+        traffic, co_bound = None, None
         tf = ROOT / "profiles" / "traffic.json"
         if tf.exists():
             try:
-                traffic = json.loads(tf.read_text()).get(args.workload, {}).get(dom_name)
+                prof = json.loads(tf.read_text()).get(args.workload, {})
+                traffic = prof.get(dom_name)
+                l1 = prof.get("l1_wavefront_frac", {}).get(dom_name)
+                if l1 is not None:
+                    co_bound = {"resource": "L1 shared-memory data pipe (table gathers)", "frac": l1,
+                                "source": "ncu --set full capture, profiles/cim_lut_kernels_gpt_m_ffn.md"}
             except ValueError:
                 traffic = None
         kernel_ms = sum(k["fwd_ms"] + k["bwd_ms"] for k in kern.values())
@@ -470,7 +475,7 @@ def run_ours(args, wl):
                     "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
                     "d2h_bytes_per_step": loss_host.numel() * loss_host.element_size()},
             "roofline": {"bound": "fp32_issue", "kernel": dom_name, "achieved": achieved / 1e12,
-                         "peak": pk / 1e12, "unit": "Tlane-op/s", "frac": achieved / pk, "traffic": traffic,
+                         "peak": pk / 1e12, "unit": "Tlane-op/s", "frac": achieved / pk, "traffic": traffic, "co_bound": co_bound,
                          "peak_source": "measured FFMA probe (cimekv_fp32_probe), sustained",
                          "peak_burst": peak["burst"] / 1e12,
                          "step_frac": value / world * (OPS_FWD + OPS_BWD) / pk,
