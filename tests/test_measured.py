@@ -81,7 +81,8 @@ def test_measured_modes_and_unit_case():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("shape,states,grid", [((300, 70, 130), 24, 33), ((1025, 37, 96), 5, 4),
-                                               ((64, 4, 32), 24, 9), ((129, 130, 1), 7, 17), ((7, 3, 65), 1, 2)])
+                                               ((64, 4, 32), 24, 9), ((129, 130, 1), 7, 17), ((7, 3, 65), 1, 2),
+                                               ((200, 40, 70), 24, 65)])  # > 1024 coefficients: large layout
 def test_measured_kernels_random_shapes(shape, states, grid):
     """Ragged tiles, inputs outside the lookup range, clamped outputs and small
     codebooks (state tables not a multiple of 4 entries), against the fp64 oracle."""
