@@ -483,6 +483,7 @@ struct FwdParams {
     int M, K, O, T;
     float dmin, scale, vsat, out_min, out_max, tia_lo, tia_hi;
     float inv, vd, i_s, di_s;  // exact-formula mode
+    int ksplit;  // 1, or 2: each tile's k range in two halves, raw sums added into a zeroed out
 };
 
 // torch.clamp semantics (NaN passes through).
@@ -563,7 +564,14 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
     const int ntiles = tiles_m * tiles_o;
     const int nchunks = (p.K + kFwdKC - 1) / kFwdKC;
 
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    // Work item = (tile, part of the k range); with ksplit == 2 the two halves of
+    // a tile add their raw sums into the zeroed output (two adds onto 0.0f give
+    // a + b in either order: deterministic) and fwd_split_epilogue_kernel clamps.
+    const int nitems = ntiles * p.ksplit;
+    for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
+        const int tile = item % ntiles, part = item / ntiles;
+        const int c_lo = (int)((int64_t)part * nchunks / p.ksplit);
+        const int c_hi = (int)((int64_t)(part + 1) * nchunks / p.ksplit);
         const int m0 = (tile / tiles_o) * kFwdMT;
         const int o0 = (tile % tiles_o) * kFwdOT;
         f32x2 acc[4][2];  // [token pair][output]
@@ -585,8 +593,8 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
                 rn[r] = (kin && go < p.O) ? __ldg(p.wn + (int64_t)go * p.K + k) : 0.0f;
             }
         };
-        if (nchunks > 0) load_chunk(0);
-        for (int c = 0; c < nchunks; ++c) {
+        if (c_hi > c_lo) load_chunk(c_lo * kFwdKC);
+        for (int c = c_lo; c < c_hi; ++c) {
             __syncthreads();  // previous chunk's readers are done with the stage
             float4 rng = make_float4(INFINITY, -INFINITY, INFINITY, -INFINITY);
             bool nan = false;
@@ -613,7 +621,7 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
             float4 tr;
             bool tnan;
             block_range4(rng, nan, red, red_nan, tr, tnan);  // includes the barrier
-            if (c + 1 < nchunks) load_chunk((c + 1) * kFwdKC);
+            if (c + 1 < c_hi) load_chunk((c + 1) * kFwdKC);
             if (kExact) {
                 fwd_chunk<false, true>(xs, is, ps, ns, lc, acc);
             } else if (tile_in_table(tr.x, tr.y, tr.z, tr.w, tnan, p.dmin, p.scale, T)) {
@@ -631,7 +639,9 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
                 const int o = o0 + lane + 32 * j;
                 float v0, v1;
                 unpk2(acc[i >> 1][j], v0, v1);
-                if (o < p.O) {
+                if (o < p.O && p.ksplit > 1) {
+                    atomicAdd(p.out + (int64_t)m * p.O + o, (i & 1) ? v1 : v0);
+                } else if (o < p.O) {
                     const float id = fminf(fmaxf((i & 1) ? v1 : v0, p.out_min), p.out_max);
                     p.out[(int64_t)m * p.O + o] = id;
                     if (p.tia_out != nullptr)  // fused TIA: the reference's `I_diff * r_tia` then clamp
@@ -639,6 +649,19 @@ __global__ void __launch_bounds__(kFwdThreads, CIMEKV_FWD_MIN_BLOCKS) fwd_kernel
                 }
             }
         }
+    }
+}
+
+// Epilogue of a k-split forward: the clamp of I_diff and the fused TIA output,
+// the same operations as the forward's own epilogue.
+__global__ void fwd_split_epilogue_kernel(float* __restrict__ out, float* __restrict__ tia_out,
+                                          const float* __restrict__ r_tia, int64_t n, float out_min,
+                                          float out_max, float tia_lo, float tia_hi) {
+    const float r = tia_out != nullptr ? __ldg(r_tia) : 0.0f;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float id = fminf(fmaxf(out[i], out_min), out_max);
+        out[i] = id;
+        if (tia_out != nullptr) tia_out[i] = clamp_keep_nan(__fmul_rn(id, r), tia_lo, tia_hi);
     }
 }
 
@@ -1200,11 +1223,29 @@ static int launch_forward(const float* x, const float* wpos, const float* wneg, 
     int resident = (int)((228 * 1024) / (smem + 1024));
     if (resident > CIMEKV_FWD_MIN_BLOCKS) resident = CIMEKV_FWD_MIN_BLOCKS;
     if (resident < 1) resident = 1;
-    long grid = (long)sms * resident;
-    if (grid > ntiles) grid = ntiles;
+    const long slots = (long)sms * resident;
+    // Split each tile's k range in two when the tiles fill the resident CTAs
+    // badly (few tiles: small per-GPU batches), e.g. 594 tiles on 444 slots run
+    // 2 waves at 67 % occupancy, 1188 half-tiles 3 waves at 89 %.
+    const int nchunks = (K + kFwdKC - 1) / kFwdKC;
+    const double eff1 = (double)ntiles / ((double)((ntiles + slots - 1) / slots) * slots);
+    const double eff2 = (double)(2 * ntiles) / ((double)((2 * ntiles + slots - 1) / slots) * slots);
+    p.ksplit = (nchunks >= 2 && eff2 > eff1 + 0.05) ? 2 : 1;
+    if (p.ksplit > 1) {
+        cudaError_t e = cudaMemsetAsync(out, 0, (size_t)M * O * sizeof(float), (cudaStream_t)stream);
+        if (e != cudaSuccess) return set_error(CIMEKV_ECUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    }
+    long grid = slots;
+    if (grid > ntiles * p.ksplit) grid = ntiles * p.ksplit;
     if (ex) fwd_kernel<true><<<(unsigned)grid, kFwdThreads, smem, (cudaStream_t)stream>>>(p);
     else fwd_kernel<false><<<(unsigned)grid, kFwdThreads, smem, (cudaStream_t)stream>>>(p);
-    return check_launch("fwd_kernel");
+    if ((rc = check_launch("fwd_kernel"))) return rc;
+    if (p.ksplit > 1) {
+        fwd_split_epilogue_kernel<<<(unsigned)(sms * 4), 256, 0, (cudaStream_t)stream>>>(
+            out, tia_out, r_tia, (int64_t)M * O, out_min, out_max, tia_lo, tia_hi);
+        return check_launch("fwd_split_epilogue_kernel");
+    }
+    return CIMEKV_OK;
 }
 
 int cimekv_forward(const float* x, const float* wpos, const float* wneg, const void* lut, int M, int K, int O,
