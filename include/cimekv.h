@@ -62,6 +62,9 @@ int cimekv_lut_pack(const uint16_t* table_i, const uint16_t* table_ddelta,
  * Replaces the reference Triton _forward_kernel launched by
  * LUTTritonEKVMatmulFn.forward (src/isa/kernels/transformer_ffn/
  * ekv_lut_triton.py:37-62,151-157); delta_scale = float((T-1)/(dmax-dmin)).
+ * For launches with few output tiles the kernel splits the k range in two and
+ * uses `out` as its accumulator (zeroed on `stream` first), so `out` must not
+ * alias an input.  The same holds for the other forward entry points.
  */
 int cimekv_forward(const float* x, const float* wpos, const float* wneg,
                    const void* lut, int M, int K, int O, int table_size,
