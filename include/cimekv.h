@@ -203,7 +203,9 @@ int cimekv_lut_index(const float* delta, int n, int table_size,
  * call.  It allocates nothing and calls no allocating routine.
  *   - The first call on a device looks up the scratch's device address
  *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture.
+ *     before any stream capture.  The address is kept for the life of the
+ *     process, so do not use the library across a cudaDeviceReset of that
+ *     device (the reset ends the context the address belongs to).
  *   - Fails with CIMEKV_EWORKSPACE when 2*out_features*in_features*4 bytes
  *     exceed the scratch (out*in > 4,194,304); larger token counts only lower
  *     the number of token splits, never the result's correctness.

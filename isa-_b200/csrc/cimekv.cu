@@ -84,6 +84,26 @@ int set_error(int code, const char* fmt, ...) {
 
 void cimekv_internal_set_error(const char* msg) { snprintf(g_last_error, sizeof(g_last_error), "%s", msg); }
 
+// Start of every entry point: clears the message of the previous call.
+int cimekv_internal_begin_call() {
+    g_last_error[0] = '\0';
+    return CIMEKV_OK;
+}
+
+// Called right before an entry point's first launch: refuses to run when a CUDA
+// error is already pending from earlier work of the process (a launch by another
+// library on this thread), so that the check after this call's own launches
+// reports only errors of this library's kernels.
+int cimekv_internal_no_pending_error() {
+    const cudaError_t e = cudaPeekAtLastError();
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();  // consume it: it belongs to earlier work, not to this call
+        return set_error(CIMEKV_ECUDA, "CUDA error pending before this call (raised by earlier work, not by "
+                         "this library): %s", cudaGetErrorString(e));
+    }
+    return CIMEKV_OK;
+}
+
 namespace {
 
 int check_launch(const char* what) {
@@ -1146,14 +1166,15 @@ size_t cimekv_lut_bytes(int table_size) {
 int cimekv_lut_pack(const uint16_t* table_i, const uint16_t* table_ddelta, int table_size, void* lut,
                     void* stream) {
     NvtxRange nvtx_range("cimekv_lut_pack");
-    g_last_error[0] = '\0';
-    int rc = check_lut_size(table_size);
+    int rc = cimekv_internal_begin_call();
+    if (rc || (rc = check_lut_size(table_size))) return rc;
     if (rc) return rc;
     if (!table_i || !table_ddelta || !lut) return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
     if (!aligned16(lut)) return set_error(CIMEKV_EINVAL_SHAPE, "lut must be 16-byte aligned");
     const int words = (int)(fwd_table_bytes(table_size) / 4);
     uint32_t* lut_i = static_cast<uint32_t*>(lut);
     uint32_t* lut_d = lut_i + words;
+    if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
     lut_pack_kernel<<<(words + 255) / 256, 256, 0, (cudaStream_t)stream>>>(table_i, table_ddelta, table_size,
                                                                             lut_i, lut_d, words);
     return check_launch("lut_pack_kernel");
@@ -1179,8 +1200,8 @@ static int launch_forward(const float* x, const float* wpos, const float* wneg, 
                           int O, int table_size, float delta_min, float delta_scale, float v_sat, float out_min,
                           float out_max, float* out, const float* r_tia, float tia_lo, float tia_hi, float* tia_out,
                           void* stream, const ExactArgs* ex = nullptr) {
-    g_last_error[0] = '\0';
-    int rc = ex ? CIMEKV_OK : check_lut_size(table_size);
+    int rc = cimekv_internal_begin_call();
+    if (rc || (rc = ex ? CIMEKV_OK : check_lut_size(table_size))) return rc;
     if (rc) return rc;
     if (M < 0 || K < 0 || O < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative size M=%d K=%d O=%d", M, K, O);
     if (M == 0 || O == 0) return CIMEKV_OK;
@@ -1231,6 +1252,7 @@ static int launch_forward(const float* x, const float* wpos, const float* wneg, 
     const double eff1 = (double)ntiles / ((double)((ntiles + slots - 1) / slots) * slots);
     const double eff2 = (double)(2 * ntiles) / ((double)((2 * ntiles + slots - 1) / slots) * slots);
     p.ksplit = (nchunks >= 2 && eff2 > eff1 + 0.05) ? 2 : 1;
+    if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
     if (p.ksplit > 1) {
         cudaError_t e = cudaMemsetAsync(out, 0, (size_t)M * O * sizeof(float), (cudaStream_t)stream);
         if (e != cudaSuccess) return set_error(CIMEKV_ECUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
@@ -1278,7 +1300,7 @@ int cimekv_tia_backward(const float* grad_out, const float* idiff, const float* 
                         float out_max, float* grad_idiff, float* grad_r_tia, void* workspace, size_t workspace_bytes,
                         void* stream) {
     NvtxRange nvtx_range("cimekv_tia_backward");
-    g_last_error[0] = '\0';
+    if (int rc0 = cimekv_internal_begin_call()) return rc0;
     if (n < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative n");
     if (!r_tia || !grad_r_tia || (n > 0 && (!grad_out || !idiff || !grad_idiff)))
         return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
@@ -1286,6 +1308,7 @@ int cimekv_tia_backward(const float* grad_out, const float* idiff, const float* 
         return set_error(CIMEKV_EWORKSPACE, "TIA backward workspace needs %zu B", (size_t)kTiaBlocks * sizeof(float));
     cudaStream_t s = (cudaStream_t)stream;
     float* partial = static_cast<float*>(workspace);
+    if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
     tia_bwd_kernel<<<kTiaBlocks, 256, 0, s>>>(grad_out, idiff, r_tia, (int64_t)n, out_min, out_max, grad_idiff,
                                               partial);
     int rc = check_launch("tia_bwd_kernel");
@@ -1306,9 +1329,8 @@ int cimekv_backward(const float* x, const float* wpos, const float* wneg, const 
                     float* grad_x, float* grad_wpos, float* grad_wneg, void* workspace, size_t workspace_bytes,
                     void* stream) {
     NvtxRange nvtx_range("cimekv_backward");
-    g_last_error[0] = '\0';
-    int rc = check_lut_size(table_size);
-    if (rc) return rc;
+    int rc = cimekv_internal_begin_call();
+    if (rc || (rc = check_lut_size(table_size))) return rc;
     if (M < 0 || K < 0 || O < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative size M=%d K=%d O=%d", M, K, O);
     if ((grad_wpos == nullptr) != (grad_wneg == nullptr))
         return set_error(CIMEKV_EINVAL_SHAPE, "grad_wpos and grad_wneg must both be given or both be NULL");
@@ -1317,6 +1339,7 @@ int cimekv_backward(const float* x, const float* wpos, const float* wneg, const 
     if (K == 0) return CIMEKV_OK;
     if (M == 0 || O == 0) {
         // Empty sums: gradients are zero.
+        if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
         if (want_w && O > 0) {
             fill_zero_kernel<<<64, 256, 0, s>>>(grad_wpos, (int64_t)O * K);
             fill_zero_kernel<<<64, 256, 0, s>>>(grad_wneg, (int64_t)O * K);
@@ -1364,6 +1387,7 @@ int cimekv_backward(const float* x, const float* wpos, const float* wneg, const 
     p.dmin = delta_min;
     p.scale = delta_scale;
     p.vsat = v_sat;
+    if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
     dim3 grid(plan.kblocks, plan.nsplit);
     if (stride == 4096) bwd_kernel<4096><<<grid, kBwdThreads, plan.smem, s>>>(p);
     else if (stride == 8192) bwd_kernel<8192><<<grid, kBwdThreads, plan.smem, s>>>(p);
@@ -1381,12 +1405,12 @@ int cimekv_backward(const float* x, const float* wpos, const float* wneg, const 
 
 int cimekv_lut_index(const float* delta, int n, int table_size, float delta_min, float delta_scale, int32_t* index,
                      float* alpha, void* stream) {
-    g_last_error[0] = '\0';
-    int rc = check_lut_size(table_size);
-    if (rc) return rc;
+    int rc = cimekv_internal_begin_call();
+    if (rc || (rc = check_lut_size(table_size))) return rc;
     if (n < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative n");
     if (n == 0) return CIMEKV_OK;
     if (!delta || !index || !alpha) return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
+    if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
     lut_index_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(delta, n, table_size, delta_min,
                                                                          delta_scale, index, alpha);
     return check_launch("lut_index_kernel");
@@ -1431,9 +1455,9 @@ extern "C" int cimekv_backward_noalloc(const float* x, const float* wpos, const 
                                        const float* grad_out, const void* lut, int M, int K, int O,
                                        int table_size, float delta_min, float delta_scale, float v_sat,
                                        float* grad_x, float* grad_wpos, float* grad_wneg, void* stream) {
-    g_last_error[0] = '\0';
-    int rc = check_lut_size(table_size);
-    if (rc) return rc;
+    NvtxRange nvtx_range("cimekv_backward_noalloc");
+    int rc = cimekv_internal_begin_call();
+    if (rc || (rc = check_lut_size(table_size))) return rc;
     if (M < 0 || K < 0 || O < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative size M=%d K=%d O=%d", M, K, O);
     if ((grad_wpos == nullptr) != (grad_wneg == nullptr))
         return set_error(CIMEKV_EINVAL_SHAPE, "grad_wpos and grad_wneg must both be given or both be NULL");
@@ -1450,6 +1474,7 @@ extern "C" int cimekv_backward_noalloc(const float* x, const float* wpos, const 
     cudaStream_t s = (cudaStream_t)stream;
     if (K == 0) return CIMEKV_OK;
     if (M == 0 || O == 0) {
+        if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
         if (want_w && O > 0) {
             fill_zero_kernel<<<64, 256, 0, s>>>(grad_wpos, (int64_t)O * K);
             fill_zero_kernel<<<64, 256, 0, s>>>(grad_wneg, (int64_t)O * K);
@@ -1498,6 +1523,7 @@ extern "C" int cimekv_backward_noalloc(const float* x, const float* wpos, const 
     p.dmin = delta_min;
     p.scale = delta_scale;
     p.vsat = v_sat;
+    if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
     dim3 grid(plan.kblocks, plan.nsplit);
     if (stride == 4096) bwd_kernel<4096><<<grid, kBwdThreads, plan.smem, s>>>(p);
     else if (stride == 8192) bwd_kernel<8192><<<grid, kBwdThreads, plan.smem, s>>>(p);
@@ -1535,7 +1561,7 @@ extern "C" int cimekv_exact_backward(const float* x, const float* wpos, const fl
                                      float* grad_x, float* grad_wpos, float* grad_wneg, void* workspace,
                                      size_t workspace_bytes, void* stream) {
     NvtxRange nvtx_range("cimekv_exact_backward");
-    g_last_error[0] = '\0';
+    if (int rc0 = cimekv_internal_begin_call()) return rc0;
     if (M < 0 || K < 0 || O < 0) return set_error(CIMEKV_EINVAL_SHAPE, "negative size M=%d K=%d O=%d", M, K, O);
     if ((grad_wpos == nullptr) != (grad_wneg == nullptr))
         return set_error(CIMEKV_EINVAL_SHAPE, "grad_wpos and grad_wneg must both be given or both be NULL");
@@ -1543,6 +1569,7 @@ extern "C" int cimekv_exact_backward(const float* x, const float* wpos, const fl
     cudaStream_t s = (cudaStream_t)stream;
     if (K == 0) return CIMEKV_OK;
     if (M == 0 || O == 0) {
+        if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
         if (want_w && O > 0) {
             fill_zero_kernel<<<64, 256, 0, s>>>(grad_wpos, (int64_t)O * K);
             fill_zero_kernel<<<64, 256, 0, s>>>(grad_wneg, (int64_t)O * K);
@@ -1589,6 +1616,7 @@ extern "C" int cimekv_exact_backward(const float* x, const float* wpos, const fl
     p.vd = ex.vd;
     p.i_s = ex.i_s;
     p.di_s = ex.di_s;
+    if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
     dim3 grid(plan.kblocks, plan.nsplit);
     bwd_kernel<0><<<grid, kBwdThreads, plan.smem, s>>>(p);
     if ((rc = check_launch("bwd_kernel<exact>"))) return rc;

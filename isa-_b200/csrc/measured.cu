@@ -25,6 +25,10 @@
 
 // Shared with cimekv.cu: records the message cimekv_last_error() returns.
 void cimekv_internal_set_error(const char* msg);
+// Shared with cimekv.cu: clears the message, fails on a CUDA error left pending by earlier work.
+int cimekv_internal_begin_call();
+// Shared with cimekv.cu: fails when a CUDA error from earlier work is pending.
+int cimekv_internal_no_pending_error();
 
 namespace {
 
@@ -388,7 +392,7 @@ extern "C" int cimekv_measured_forward(const float* x, const int16_t* pos_idx, c
                                        const float* vg, const float* coef, int M, int K, int O, int S, int G,
                                        float lookup_min, float lookup_max, const float* r_tia, float out_min,
                                        float out_max, float* idiff, float* out, void* stream) {
-    cimekv_internal_set_error("");
+    if (int rc0 = cimekv_internal_begin_call()) return rc0;
     MeasParams p = make_params(x, pos_idx, neg_idx, vg, coef, M, K, O, S, G, lookup_min, lookup_max, r_tia,
                                out_min, out_max, idiff, out);
     int rc = check_args(p);
@@ -399,6 +403,7 @@ extern "C" int cimekv_measured_forward(const float* x, const int16_t* pos_idx, c
     const long tiles = (long)((M + kMT - 1) / kMT) * ((O + kOT - 1) / kOT);
     long grid = (long)sms * CIMEKV_MEAS_FWD_CTAS;
     if (grid > tiles) grid = tiles;
+    if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
     if (fwd_ic_off(p) == kIcOffSmall)
         measured_fwd_kernel<kIcOffSmall><<<(unsigned)grid, kThreads, smem, (cudaStream_t)stream>>>(p);
     else
@@ -412,7 +417,7 @@ extern "C" int cimekv_measured_backward_x(const float* x, const int16_t* pos_idx
                                           float lookup_min, float lookup_max, const float* r_tia, float out_min,
                                           float out_max, const float* idiff, const float* grad_out,
                                           float* grad_x, void* stream) {
-    cimekv_internal_set_error("");
+    if (int rc0 = cimekv_internal_begin_call()) return rc0;
     MeasParams p = make_params(x, pos_idx, neg_idx, vg, coef, M, K, O, S, G, lookup_min, lookup_max, r_tia,
                                out_min, out_max, const_cast<float*>(idiff), grad_x);
     int rc = check_args(p);
@@ -428,6 +433,7 @@ extern "C" int cimekv_measured_backward_x(const float* x, const int16_t* pos_idx
     int nsplit = (8 * kDxMinBlocks * sms + kgroups - 1) / kgroups;  // ~8 waves: small tail
     if (nsplit > tiles_m) nsplit = tiles_m;
     if (nsplit < 1) nsplit = 1;
+    if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
     measured_dx_kernel<<<dim3((unsigned)kgroups, (unsigned)nsplit), kThreads, smem, (cudaStream_t)stream>>>(
         p, grad_out, grad_x, nsplit);
     cudaError_t e = cudaGetLastError();

@@ -210,8 +210,15 @@ def test_partial_gradients_and_determinism():
 
 
 def test_nan_inputs_follow_the_oracle():
-    """A NaN input poisons its own row/column sums and nothing else (and the
-    kernels take the clamped path for the tile that holds it)."""
+    """NaN inputs, as the reference's index rule and clamps treat them.
+    A NaN threshold (wpos[5,2]) gives a NaN table coordinate, which the
+    coordinate clamp (fminf/fmaxf, like tl.minimum/tl.maximum) turns into entry
+    0 with weight 0: a finite lookup.  A NaN input (x[3,7]) also makes its
+    velocity-saturation factor NaN, so every sum with that factor is NaN.
+    Forward: row 3's I_diff sums are NaN and the output clamp (fminf/fmaxf
+    again) turns them into out_min (-4); all other outputs match the oracle.
+    Backward (no output clamp): dX is NaN only at (3,7), dVth_pos and dVth_neg
+    in input column 7; everything else is finite and matches the oracle."""
     tib, tdb, dmin, scale, size = cfg_tables(4096)
     lut = pack(tib, tdb)
     rng = np.random.default_rng(5)
@@ -224,16 +231,28 @@ def test_nan_inputs_follow_the_oracle():
     g = rng.standard_normal((m, o)).astype(np.float32)
     out = gpu_forward(x, wp, wn, lut, dmin, scale, size)
     ref = oracle.forward(x, wp, wn, bf16_bits_to_f32(tib), dmin, scale, CFG_V_SAT)
-    np.testing.assert_array_equal(np.isnan(out), np.isnan(ref))
-    ok = ~np.isnan(ref)
+    touched = np.zeros((m, o), dtype=bool)
+    touched[3, :] = True
+    assert not np.isnan(out).any() and not np.isnan(ref).any()
+    np.testing.assert_array_equal(out[touched], np.float32(-4.0))
+    np.testing.assert_array_equal(ref[touched], np.float32(-4.0))
     _, mag = oracle.forward(np.nan_to_num(x), np.nan_to_num(wp), wn, bf16_bits_to_f32(tib), dmin, scale,
                             CFG_V_SAT, with_mag=True)
-    assert_close_scaled(np.where(ok, out, 0), np.where(ok, ref, 0), mag, what="NaN-free outputs")
+    assert_close_scaled(np.where(touched, 0, out), np.where(touched, 0, ref), mag, what="untouched outputs")
     gx, gwp, gwn = gpu_backward(x, wp, wn, g, lut, dmin, scale, size)
     rx, rwp, rwn = oracle.backward(x, wp, wn, g, bf16_bits_to_f32(tib), bf16_bits_to_f32(tdb), dmin, scale,
                                    CFG_V_SAT)
-    for a, b in ((gx, rx), (gwp, rwp), (gwn, rwn)):
-        np.testing.assert_array_equal(np.isnan(a), np.isnan(b))
+    kk_x = np.arange(k)[None, :]
+    want_x = np.zeros((m, k), dtype=bool)
+    want_x[3, 7] = True
+    want_p = np.broadcast_to(kk_x == 7, (o, k))
+    want_n = np.broadcast_to(kk_x == 7, (o, k))
+    for got, exp, want, name in ((gx, rx, want_x, "dX"), (gwp, rwp, want_p, "dVth_pos"), (gwn, rwn, want_n, "dVth_neg")):
+        np.testing.assert_array_equal(np.isnan(got), want, err_msg=name)
+        np.testing.assert_array_equal(np.isnan(exp), want, err_msg=f"oracle {name}")
+        scale_ = np.abs(np.where(want, 0, exp)).max()
+        np.testing.assert_allclose(np.where(want, 0, got), np.where(want, 0, exp), rtol=1e-4, atol=1e-5 * scale_,
+                                   err_msg=name)
 
 
 @pytest.mark.parametrize("shape", [(1, 384, 1536), (4096, 1, 7), (33, 5, 1)])
