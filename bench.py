@@ -72,6 +72,9 @@ def parse():
     ap.add_argument("--cpu-sample-tokens", type=int, default=1024,
                     help="tokens of the CPU baseline sample (our arm)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the GPT-L step sub-record and the reference-GPU comparison of the default line")
+    ap.add_argument("--gpt-l-steps", type=int, default=3, help="timed steps of the GPT-L sub-record")
     return ap.parse_args()
 
 
@@ -140,6 +143,15 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- helpers ----
+
+def host_cores() -> int:
+    """Host threads this process may use (its CPU affinity), independent of
+    OMP_NUM_THREADS, which torchrun sets to 1 for every rank."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
 
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
@@ -329,6 +341,55 @@ def reference_pytorch_cpu(wl, tokens=64, seed=0) -> dict:
 
 # ------------------------------------------------------------ our arm -----
 
+def extras_wanted(args) -> bool:
+    return args.impl == "ours" and args.workload == "gpt_m_ffn" and not args.no_extras
+
+
+def _bench_subprocess(argv, timeout=900) -> dict:
+    """One bench.py invocation in a fresh process; its JSON line, or why not."""
+    cmd = [sys.executable, str(ROOT / "bench.py"), *argv, "--no-cpu-baseline", "--no-extras"]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, cwd=str(ROOT),
+                           env={**os.environ, "WORLD_SIZE": "1", "RANK": "0", "LOCAL_RANK": "0"})
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"timed out after {timeout} s: {' '.join(argv)}"}
+    for line in reversed(r.stdout.splitlines()):
+        if line.startswith("{"):
+            try:
+                return json.loads(line)
+            except ValueError:
+                break
+    tail = (r.stderr or r.stdout).strip().splitlines()[-1:] or ["no output"]
+    return {"unavailable": f"exit {r.returncode}: {tail[0][:300]}"}
+
+
+def reference_gpu_comparison(args, ours_rec) -> dict:
+    """The reference's own GPU path (unmodified package in baseline/_ref: Triton
+    LUT forward, JIT-built CUDA shared backward) on the same GPU and workload,
+    Physical (config 3) and Hybrid (config 3, Hybrid variant), each in a
+    subprocess; with our/reference ratios of the device-timed step rates."""
+    if not (ROOT / "baseline" / "_ref" / "isa").exists():
+        return {"unavailable": "baseline/_ref (the pip-installed reference) is not present"}
+    steps, warm = str(min(args.steps, 10)), str(max(args.warmup, 3))
+    out = {}
+    ref_p = _bench_subprocess(["--impl", "reference_gpu", "--workload", "gpt_m_ffn", "--steps", steps,
+                               "--warmup", warm])
+    ours_h = _bench_subprocess(["--impl", "ours", "--workload", "gpt_m_ffn_hybrid", "--steps", steps,
+                                "--warmup", warm])
+    ref_h = _bench_subprocess(["--impl", "reference_gpu", "--workload", "gpt_m_ffn_hybrid", "--steps", steps,
+                               "--warmup", warm])
+    for key, ref, ours in (("physical", ref_p, ours_rec), ("hybrid", ref_h, ours_h)):
+        ent = {"reference": {k: ref.get(k) for k in ("value", "unit", "ms_per_step", "clocks", "unavailable")
+                             if k in ref},
+               "ours": {k: ours.get(k) for k in ("value", "unit", "ms_per_step", "unavailable") if k in ours}}
+        if "value" in ref and "value" in ours:
+            ent["ratio_ours_over_reference"] = ours["value"] / ref["value"]
+        out[key] = ent
+    out["note"] = ("reference: unmodified package from baseline/_ref through its module API (Triton _forward_kernel, "
+                   "CUDA grad_x_shared/grad_w_shared), same workload, same device-event timing")
+    return out
+
+
 def run_ours(args, wl):
     import torch
     import torch.distributed as dist
@@ -403,12 +464,20 @@ def run_ours(args, wl):
     e2e_value = world * cells_step * args.steps / (float(e_ms.item()) * 1e-3)
 
     kern = time_kernels(ffn, cfg, x, dev) if rank == 0 and not refgpu and not exact else None
+    # Second half of the headline metric, measured in the same invocation on the
+    # same ranks: the Physical GPT-L training step at a fixed global batch.
+    gpt_l = None
+    if extras_wanted(args) and not refgpu and not exact and not wl.get("hybrid"):
+        del ffn
+        torch.cuda.empty_cache()
+        gpt_l = gpt_l_measure(WORKLOADS["gpt_l_step"], world, rank, local, dev, args.gpt_l_steps,
+                              min(args.warmup, 3))
     peak = fp32_peak(dev) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not refgpu and not exact:
-        from oracle import oracle
-        c, sec = cpu_sample(wl, args.cpu_sample_tokens)
-        cpu = {"value": c / sec / 1e9, "unit": "Gcell-evals/s", "cores": oracle.max_threads(), "kind": "port",
+        cores = host_cores()
+        c, sec = cpu_sample(wl, args.cpu_sample_tokens, nthreads=cores)
+        cpu = {"value": c / sec / 1e9, "unit": "Gcell-evals/s", "cores": cores, "kind": "port",
                "sample": f"{args.cpu_sample_tokens} tokens of the block (both projections, fwd+bwd), "
                          f"oracle/cimekv_oracle.c with OpenMP, {sec:.1f} s"}
     cpu_ref = None
@@ -448,7 +517,8 @@ def run_ours(args, wl):
                 l1 = prof.get("l1_wavefront_frac", {}).get(dom_name)
                 if l1 is not None:
                     co_bound = {"resource": "L1 shared-memory data pipe (table gathers)", "frac": l1,
-                                "source": "ncu --set full capture, profiles/cim_lut_kernels_gpt_m_ffn.md"}
+                                "source": "ncu capture of this kernel, profiles/traffic.json",
+                                "captured_at_commit": prof.get("commit")}
             except ValueError:
                 traffic = None
         kernel_ms = sum(k["fwd_ms"] + k["bwd_ms"] for k in kern.values())
@@ -489,6 +559,10 @@ def run_ours(args, wl):
             "gpu_launches": 10 * args.steps,  # per projection: fwd, tia_bwd, sum_partials, bwd, bwd_reduce
             "impl": "ours",
         }
+        if gpt_l is not None:
+            rec["gpt_l_step"] = gpt_l
+        if extras_wanted(args) and world == 1:
+            rec["reference_gpu"] = reference_gpu_comparison(args, rec)
         print(json.dumps(rec), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -500,18 +574,17 @@ def run_reference(args, wl):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # rank 0 alone times the host CPU path
-    from oracle import oracle
 
     tokens = 128  # bounded sample per step: ~1 s of CPU work on 8 cores
     for _ in range(max(args.warmup, 1)):
-        cpu_sample(wl, tokens)
+        cpu_sample(wl, tokens, nthreads=host_cores())
     total_c, total_s = 0, 0.0
     for i in range(args.steps):
-        c, s = cpu_sample(wl, tokens, seed=i)
+        c, s = cpu_sample(wl, tokens, nthreads=host_cores(), seed=i)
         total_c += c
         total_s += s
     v = total_c / total_s / 1e9
-    cores = oracle.max_threads()
+    cores = host_cores()
     rec = {
         "metric": "CIM-FFN fwd+bwd Gcell-evals/s", "value": v, "unit": "Gcell-evals/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_s * 1e3 / args.steps,
@@ -597,21 +670,15 @@ def run_vit_l(args, wl):
         dist.destroy_process_group()
 
 
-def run_gpt_l(args, wl):
+def gpt_l_measure(wl, world, rank, local, dev, steps, warmup):
     """Full Physical GPT-L training step (forward, backward, DDP all-reduce,
-    clip, AdamW, clamp_vth); the global batch is fixed, split across ranks."""
+    clip, AdamW, clamp_vth); the global batch is fixed and split across the
+    ranks of the (already initialised) process group.  Returns rank 0's record."""
     import torch
     import torch.distributed as dist
 
     from isa_b200.harness.gpt import GPTConfig, PhysicalGPT, train_step
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
     if wl["batch"] % world:
         raise SystemExit(f"global batch {wl['batch']} does not split over {world} ranks")
     per = wl["batch"] // world
@@ -631,10 +698,10 @@ def run_gpt_l(args, wl):
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(max(warmup, 2)):
         train_step(net, opt, ids, cims)
     barrier()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     loss_host = torch.empty((), pin_memory=True)
     with ClockSampler(torch.cuda.current_device()) as clocks:
         barrier()
@@ -650,22 +717,39 @@ def run_gpt_l(args, wl):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    tokens = wl["batch"] * wl["seq"] * args.steps
-    if rank == 0:
-        cells = tokens * wl["layers"] * cells_per_token(wl)
-        rec = {"metric": "Physical GPT-L train tokens/s", "value": tokens / (ms * 1e-3), "unit": "tokens/s",
-               "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-               "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 CIM / bf16 digital",
-               "data": "synthetic token ids uniform in [0, 50257), random-init weights",
-               "config": {"workload": "gpt_l_step", "model": wl["model"], "global_batch": wl["batch"],
-                          "seq_len": wl["seq"], "parallelism": f"dp{world}", "lut_size": wl["lut"],
-                          "l2": "working set >> L2 (activations of 64k tokens)"},
-               "cim_gcell_evals_per_s": cells / (ms * 1e-3) / 1e9,
-               "e2e": {"value": tokens / (ms * 1e-3), "unit": "tokens/s",
-                       "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(),
-                       "d2h_bytes_per_step": 4},
-               "loss": float(loss_host), "clocks": clocks.summary(),
-               "gpu_launches": 10 * wl["layers"] * args.steps, "impl": "ours"}
+    tokens = wl["batch"] * wl["seq"] * steps
+    del net, model, opt
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    cells = tokens * wl["layers"] * cells_per_token(wl)
+    return {"metric": "Physical GPT-L train tokens/s", "value": tokens / (ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": max(warmup, 2), "ms_per_step": ms / steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 CIM / bf16 digital",
+            "data": "synthetic token ids uniform in [0, 50257), random-init weights",
+            "config": {"workload": "gpt_l_step", "model": wl["model"], "global_batch": wl["batch"],
+                       "per_gpu_batch": per, "seq_len": wl["seq"], "parallelism": f"dp{world}",
+                       "lut_size": wl["lut"], "l2": "working set >> L2 (activations of 64k tokens)"},
+            "cim_gcell_evals_per_s": cells / (ms * 1e-3) / 1e9,
+            "e2e": {"value": tokens / (ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(), "d2h_bytes_per_step": 4},
+            "loss": float(loss_host), "clocks": clocks.summary(),
+            "gpu_launches": 10 * wl["layers"] * steps, "impl": "ours"}
+
+
+def run_gpt_l(args, wl):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    rec = gpt_l_measure(wl, world, rank, local, dev, args.steps, args.warmup)
+    if rec is not None:
         print(json.dumps(rec), flush=True)
     if world > 1:
         dist.destroy_process_group()

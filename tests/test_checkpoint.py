@@ -40,3 +40,17 @@ def test_checkpoint_round_trip_and_cross_load():
     from isa_b200.operators.measured import DeploymentAwareCIMLinear
     layer = DeploymentAwareCIMLinear.from_cimlinear(src.fc1)
     assert torch.equal(layer.vth_pos, src.fc1.vth_pos)
+
+
+def test_language_model_layout_matches_reference():
+    """GPT2Model with hybrid / physical FFNs: the same state-dict keys, shapes and
+    dtypes as the reference GPT2Model (fixture by
+    tests/golden/make_language_layout.py), so the GPT-side wrappers (HybridFFN's
+    ``cim1``, GPT2PhysicalFFN's ``cim_ffn``) load reference checkpoints."""
+    from isa_b200.language import GPT2Model, ModelConfig
+    ref = json.loads((GOLDEN / "reference_language_state_dict_layout.json").read_text())
+    for kind in ("hybrid", "physical"):
+        cfg = ModelConfig.from_preset("tiny", kind, max_seq_len=64)
+        cfg.depth = 2
+        got = {k: [list(v.shape), str(v.dtype)] for k, v in GPT2Model(cfg).state_dict().items()}
+        assert got == ref[kind], kind

@@ -41,8 +41,20 @@ def _run(x, wp, wn, g, lut, dmin, scale, size):
     return out, gx, gwp, gwn
 
 
-@pytest.mark.parametrize("shape,size", [((32768, 384, 1536), 4096), ((32768, 1536, 384), 4096),
-                                        ((8320, 256, 1024), 8192)])
+# Layer shapes of the benchmark configs, at the token counts one GPU sees:
+#   config 3 (GPT-M FFN block, 32x1024 tokens), config 2 (ViT-M block, 128x65),
+#   config 4 (GPT-L: 768 <-> 3072, 64x1024 tokens on 1 GPU, 8x1024 per GPU at 8),
+#   config 5 (ViT-L: 384 <-> 1536, 256x197 tokens on 1 GPU, 32x197 per GPU at 8).
+# The config-4 up projection at 8 GPUs combines the forward's k split (few
+# tiles) with the backward's workspace dVth accumulator (O = 3072).
+FULL_SHAPES = [
+    ((32768, 384, 1536), 4096), ((32768, 1536, 384), 4096), ((8320, 256, 1024), 8192),
+    ((65536, 768, 3072), 4096), ((65536, 3072, 768), 4096), ((8192, 768, 3072), 4096), ((8192, 3072, 768), 4096),
+    ((50432, 384, 1536), 8192), ((50432, 1536, 384), 8192), ((6304, 384, 1536), 8192), ((6304, 1536, 384), 8192),
+]
+
+
+@pytest.mark.parametrize("shape,size", FULL_SHAPES, ids=[f"{m}x{k}x{o}-T{t}" for (m, k, o), t in FULL_SHAPES])
 def test_fullsize_rows_match_oracle_and_dvth_is_additive(shape, size):
     m, k, o = shape
     tib, tdb, dmin, scale, _ = cfg_tables(size)
