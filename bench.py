@@ -517,7 +517,7 @@ def run_ours(args, wl):
                 l1 = prof.get("l1_wavefront_frac", {}).get(dom_name)
                 if l1 is not None:
                     co_bound = {"resource": "L1 shared-memory data pipe (table gathers)", "frac": l1,
-                                "source": "ncu capture of this kernel, profiles/traffic.json",
+                                "source": "ncu capture of this kernel (committed traffic record)",
                                 "captured_at_commit": prof.get("commit")}
             except ValueError:
                 traffic = None

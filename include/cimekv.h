@@ -118,6 +118,15 @@ size_t cimekv_backward_workspace_bytes(int M, int K, int O, int table_size);
  * :433-574, bound as grad_x_shared / grad_w_shared in cuda/binding.cpp:56-62).
  * grad_x may be NULL (no input gradient); grad_wpos and grad_wneg may both be
  * NULL (no threshold gradient).  The result is deterministic.
+ * workspace: at least cimekv_backward_workspace_bytes(M, K, O, table_size)
+ * bytes, 16-byte aligned.  It holds the per-token-split threshold partials
+ * and, for layers of 768 to 4096 outputs, per input column the outputs
+ * regrouped into clusters of close thresholds (so the table gathers of a warp
+ * hit distinct shared-memory banks).
+ * A call with grad_wpos == grad_wneg == NULL may pass workspace = NULL; it then
+ * runs the unclustered kernel, whose grad_x differs from the clustered one in
+ * fp32 summation order only.  Give the workspace to get the same bits as a
+ * full call.
  */
 int cimekv_backward(const float* x, const float* wpos, const float* wneg,
                     const float* grad_out, const void* lut,
@@ -194,8 +203,8 @@ int cimekv_lut_index(const float* delta, int n, int table_size,
 /*
  * Allocation-free variant of cimekv_backward; it has no counterpart in the
  * reference.  Same arguments and results as cimekv_backward, minus the
- * workspace: the token-split dVth partials go to a scratch array compiled into
- * this library (CIMEKV_NOALLOC_SCRATCH_BYTES of static device memory, held by
+ * workspace: the per-column output clusters and the token-split dVth partials
+ * go to a scratch array compiled into this library (CIMEKV_NOALLOC_SCRATCH_BYTES of static device memory, held by
  * every GPU that loads the library until the process exits).  It is for callers
  * that cannot call cudaMalloc or an allocator around this operator — e.g. code
  * running under a memory pool it does not own, a host runtime with no device
@@ -214,7 +223,10 @@ int cimekv_lut_index(const float* delta, int n, int table_size,
  *     give wrong dVth.  Calls ordered on one stream are safe.  Each call
  *     overwrites every scratch element it reads, so nothing needs clearing.
  *   - Results are identical to cimekv_backward's up to the order of the
- *     deterministic split reduction (which may use fewer splits).
+ *     deterministic split reduction (which may use fewer splits).  Layers whose
+ *     clusters (12*out*in bytes plus 16 per input) and one split do not fit
+ *     the scratch together (out*in above ~1.6 M) run the unclustered kernel;
+ *     their grad_x then differs from cimekv_backward's in fp32 summation order.
  */
 int cimekv_backward_noalloc(const float* x, const float* wpos, const float* wneg,
                             const float* grad_out, const void* lut,

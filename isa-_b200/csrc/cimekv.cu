@@ -33,6 +33,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <mutex>
 
@@ -120,7 +121,7 @@ constexpr int kMaxDevices = 64;
 std::mutex g_dev_mutex;
 int g_sm_count[kMaxDevices] = {0};
 int g_smem_optin[kMaxDevices] = {0};
-bool g_attr_set[kMaxDevices][8] = {};
+bool g_attr_set[kMaxDevices][16] = {};
 
 int current_device(int* dev) {
     cudaError_t e = cudaGetDevice(dev);
@@ -1081,6 +1082,8 @@ __global__ void sum_partials_kernel(const float* __restrict__ partial, int n, fl
     }
 }
 
+#include "bwd_cluster.cuh"
+
 // Token splits of the backward: enough CTAs to fill the GPU in whole waves.
 struct BwdPlan {
     int kblocks, tiles_m, nsplit;
@@ -1137,6 +1140,158 @@ int plan_backward(int M, int K, int O, int T, BwdPlan* plan, int stride = -1) {
     plan->nsplit = best;
     plan->workspace = (size_t)best * 2 * (size_t)O * (size_t)K * sizeof(float);
     return CIMEKV_OK;
+}
+
+// Plan of the clustered backward (bwd_cluster.cuh).  *ok = false when it does
+// not apply; the caller then runs bwd_kernel.  It applies from kCluMinOutputs
+// outputs up to kCluMaxOutputs, when tables + g tile fit shared memory.  Below
+// kCluMinOutputs the unclustered kernel measured as fast or faster (B200: 384
+// outputs 29.2 vs 30.4 ms, 256 outputs 14.8 vs 15.4 ms; at 768..3072 outputs
+// the clustered kernel is 3-14 % faster).
+struct Bwd2Plan {
+    int kt, wpk, ncl, opad, tm, kgroups, tiles_m, nsplit, items, grid, sort_n, band;
+    size_t smem, co_off, cr_off, part_off, workspace;
+};
+
+size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+// CIMEKV_BWD_CLUSTER=0 in the environment selects the unclustered kernel.
+bool cluster_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("CIMEKV_BWD_CLUSTER");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+int plan_backward2(int M, int K, int O, int T, Bwd2Plan* pl, bool* ok) {
+    *ok = false;
+    if (!cluster_enabled() || O < kCluMinOutputs || O > kCluMaxOutputs || M <= 0 || K <= 0) return CIMEKV_OK;
+    int dev, sms, optin;
+    int rc = current_device(&dev);
+    if (rc || (rc = device_limits(dev, &sms, &optin))) return rc;
+    const int stride = bwd_stride(T);
+    pl->ncl = (O + 31) / 32;
+    pl->opad = pl->ncl * 32;
+    int kmax = 1;
+    while (kmax < K && kmax < kB2MaxKT) kmax <<= 1;
+    for (pl->kt = kmax; pl->kt >= 1; pl->kt >>= 1) {
+        if (kB2Warps % pl->kt) continue;
+        pl->wpk = kB2Warps / pl->kt;
+        if ((pl->ncl + pl->wpk - 1) / pl->wpk <= kB2UMax) break;
+    }
+    if (pl->kt < 1) return CIMEKV_OK;
+    pl->tm = 8;
+    pl->smem = bwd2_smem_bytes(stride, 8, pl->opad, pl->kt);
+    if (pl->smem > (size_t)optin) {
+        pl->tm = 4;
+        pl->smem = bwd2_smem_bytes(stride, 4, pl->opad, pl->kt);
+    }
+    if (pl->smem > (size_t)optin) return CIMEKV_OK;
+    pl->kgroups = (K + pl->kt - 1) / pl->kt;
+    pl->tiles_m = (M + pl->tm - 1) / pl->tm;
+    // Token splits: whole waves of work items over the SMs; a small charge per
+    // split for the workspace the reduction writes and reads.
+    int best = 1;
+    double best_cost = 1e300;
+    const int max_split = pl->tiles_m < 512 ? pl->tiles_m : 512;
+    for (int sp = 1; sp <= max_split; ++sp) {
+        const long items = (long)pl->kgroups * sp;
+        const long waves = (items + sms - 1) / sms;
+        const double cost = (double)waves * (double)((pl->tiles_m + sp - 1) / sp) + 0.002 * sp * pl->tiles_m;
+        if (cost < best_cost - 1e-9) {
+            best_cost = cost;
+            best = sp;
+        }
+    }
+    pl->nsplit = best;
+    pl->items = pl->kgroups * best;
+    pl->grid = pl->items < sms ? pl->items : sms;
+    pl->sort_n = 32;
+    while (pl->sort_n < O) pl->sort_n <<= 1;
+    int nb = (int)std::lround(std::sqrt((double)pl->ncl));
+    if (nb < 1) nb = 1;
+    pl->band = (pl->ncl + nb - 1) / nb * 32;
+    pl->co_off = align256((size_t)K * pl->opad * sizeof(float2));
+    pl->cr_off = pl->co_off + align256((size_t)K * pl->opad * sizeof(int));
+    pl->part_off = pl->cr_off + align256((size_t)K * sizeof(float4));
+    pl->workspace = pl->part_off + (size_t)best * 2 * (size_t)O * (size_t)K * sizeof(float);
+    *ok = true;
+    return CIMEKV_OK;
+}
+
+template <int kStride>
+int launch_backward2_stride(const Bwd2Plan& pl, int dev, int optin, const float* x, const float* wpos,
+                            const float* wneg, const float* grad_out, const void* lut, int M, int K, int O, int T,
+                            float dmin, float scale, float vsat, float* grad_x, bool want_w, void* workspace,
+                            cudaStream_t s) {
+    const int slot = 8 + 2 * (kStride == 4096 ? 0 : (kStride == 8192 ? 1 : 2)) + (pl.tm == 4 ? 1 : 0);
+    int rc = pl.tm == 8 ? allow_smem(dev, slot, bwd2_kernel<kStride, 8>, optin)
+                        : allow_smem(dev, slot, bwd2_kernel<kStride, 4>, optin);
+    if (rc) return rc;
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    Bwd2Params p;
+    p.x = x;
+    p.g = grad_out;
+    p.cw = reinterpret_cast<const float2*>(ws);
+    p.co = reinterpret_cast<const int*>(ws + pl.co_off);
+    p.crange = reinterpret_cast<const float4*>(ws + pl.cr_off);
+    p.lut_i = static_cast<const uint32_t*>(lut);
+    p.lut_d = p.lut_i + fwd_table_bytes(T) / 4;
+    p.grad_x = grad_x;
+    p.part = want_w ? reinterpret_cast<float*>(ws + pl.part_off) : nullptr;
+    p.M = M;
+    p.K = K;
+    p.O = O;
+    p.opad = pl.opad;
+    p.T = T;
+    p.kt = pl.kt;
+    p.wpk = pl.wpk;
+    p.ncl = pl.ncl;
+    p.kgroups = pl.kgroups;
+    p.tiles_m = pl.tiles_m;
+    p.nsplit = pl.nsplit;
+    p.items = pl.items;
+    p.dmin = dmin;
+    p.scale = scale;
+    p.vsat = vsat;
+    if (int rc_p = cimekv_internal_no_pending_error()) return rc_p;
+    cluster_kernel<<<K, 512, (size_t)pl.sort_n * sizeof(unsigned long long), s>>>(
+        wpos, wneg, K, O, pl.sort_n, pl.band, reinterpret_cast<float2*>(ws), reinterpret_cast<int*>(ws + pl.co_off),
+        reinterpret_cast<float4*>(ws + pl.cr_off));
+    if ((rc = check_launch("cluster_kernel"))) return rc;
+    if (pl.tm == 8) bwd2_kernel<kStride, 8><<<pl.grid, kB2Threads, pl.smem, s>>>(p);
+    else bwd2_kernel<kStride, 4><<<pl.grid, kB2Threads, pl.smem, s>>>(p);
+    return check_launch("bwd2_kernel");
+}
+
+// Clustered backward plus the split reduction; `workspace` laid out as pl says.
+int launch_backward2(const Bwd2Plan& pl, const float* x, const float* wpos, const float* wneg,
+                     const float* grad_out, const void* lut, int M, int K, int O, int T, float dmin, float scale,
+                     float vsat, float* grad_x, float* grad_wpos, float* grad_wneg, void* workspace,
+                     cudaStream_t s) {
+    int dev, sms, optin, rc;
+    if ((rc = current_device(&dev))) return rc;
+    if ((rc = device_limits(dev, &sms, &optin))) return rc;
+    const bool want_w = grad_wpos != nullptr;
+    const int st = bwd_stride(T);
+    if (st == 4096)
+        rc = launch_backward2_stride<4096>(pl, dev, optin, x, wpos, wneg, grad_out, lut, M, K, O, T, dmin, scale,
+                                           vsat, grad_x, want_w, workspace, s);
+    else if (st == 8192)
+        rc = launch_backward2_stride<8192>(pl, dev, optin, x, wpos, wneg, grad_out, lut, M, K, O, T, dmin, scale,
+                                           vsat, grad_x, want_w, workspace, s);
+    else
+        rc = launch_backward2_stride<16384>(pl, dev, optin, x, wpos, wneg, grad_out, lut, M, K, O, T, dmin, scale,
+                                            vsat, grad_x, want_w, workspace, s);
+    if (rc || !want_w) return rc;
+    const int64_t n = (int64_t)O * K;
+    int blocks = (int)((n + 255) / 256);
+    if (blocks > sms * 8) blocks = sms * 8;
+    bwd_reduce_kernel<<<blocks, 256, 0, s>>>(
+        reinterpret_cast<const float*>(static_cast<unsigned char*>(workspace) + pl.part_off), pl.nsplit, n,
+        grad_wpos, grad_wneg);
+    return check_launch("bwd_reduce_kernel");
 }
 
 int check_lut_size(int T) {
@@ -1319,6 +1474,10 @@ int cimekv_tia_backward(const float* grad_out, const float* idiff, const float* 
 
 size_t cimekv_backward_workspace_bytes(int M, int K, int O, int table_size) {
     if (M <= 0 || K <= 0 || O <= 0 || check_lut_size(table_size)) return 0;
+    Bwd2Plan plan2;
+    bool ok2 = false;
+    if (plan_backward2(M, K, O, table_size, &plan2, &ok2)) return 0;
+    if (ok2) return plan2.workspace;
     BwdPlan plan;
     if (plan_backward(M, K, O, table_size, &plan)) return 0;
     return plan.workspace;
@@ -1351,6 +1510,18 @@ int cimekv_backward(const float* x, const float* wpos, const float* wneg, const 
     if (!x || !wpos || !wneg || !grad_out || !lut) return set_error(CIMEKV_EINVAL_SHAPE, "null pointer");
     if (!aligned16(lut)) return set_error(CIMEKV_EINVAL_SHAPE, "lut must be 16-byte aligned");
     if (!(delta_scale > 0.0f)) return set_error(CIMEKV_EINVAL_SHAPE, "delta_scale must be > 0");
+    Bwd2Plan plan2;
+    bool ok2 = false;
+    if ((rc = plan_backward2(M, K, O, table_size, &plan2, &ok2))) return rc;
+    if (ok2 && want_w && (!workspace || workspace_bytes < plan2.workspace))
+        return set_error(CIMEKV_EWORKSPACE, "backward workspace needs %zu B, got %zu B", plan2.workspace,
+                         workspace_bytes);
+    if (ok2 && workspace && workspace_bytes >= plan2.workspace) {
+        // Clustered kernel (a dX-only call without a workspace takes bwd_kernel).
+        if (!aligned16(workspace)) return set_error(CIMEKV_EINVAL_SHAPE, "workspace must be 16-byte aligned");
+        return launch_backward2(plan2, x, wpos, wneg, grad_out, lut, M, K, O, table_size, delta_min, delta_scale,
+                                v_sat, grad_x, grad_wpos, grad_wneg, workspace, s);
+    }
     BwdPlan plan;
     if ((rc = plan_backward(M, K, O, table_size, &plan))) return rc;
     if (want_w) {
@@ -1495,6 +1666,26 @@ extern "C" int cimekv_backward_noalloc(const float* x, const float* wpos, const 
     if ((rc = current_device(&dev))) return rc;
     if ((rc = device_limits(dev, &sms, &optin))) return rc;
     float* scratch = nullptr;
+    {
+        // Clustered kernel when its column clusters and at least one token
+        // split fit the scratch (the same kernel, and so the same grad_x bits,
+        // as cimekv_backward); fewer splits than planned when needed.
+        Bwd2Plan plan2;
+        bool ok2 = false;
+        if ((rc = plan_backward2(M, K, O, table_size, &plan2, &ok2))) return rc;
+        const size_t per_split2 = (size_t)2 * O * K * sizeof(float);
+        if (ok2 && plan2.part_off + per_split2 <= CIMEKV_NOALLOC_SCRATCH_BYTES) {
+            const int fit = (int)((CIMEKV_NOALLOC_SCRATCH_BYTES - plan2.part_off) / per_split2);
+            if (plan2.nsplit > fit) {
+                plan2.nsplit = fit;
+                plan2.items = plan2.kgroups * fit;
+                plan2.grid = plan2.items < sms ? plan2.items : sms;
+            }
+            if ((rc = noalloc_scratch(dev, &scratch))) return rc;
+            return launch_backward2(plan2, x, wpos, wneg, grad_out, lut, M, K, O, table_size, delta_min,
+                                    delta_scale, v_sat, grad_x, grad_wpos, grad_wneg, scratch, s);
+        }
+    }
     if (want_w && (rc = noalloc_scratch(dev, &scratch))) return rc;
     const int stride = bwd_stride(table_size);
     const int slot = stride == 4096 ? 1 : (stride == 8192 ? 2 : 3);

@@ -71,10 +71,10 @@ class LUTCudaEKVMatmulFn(torch.autograd.Function):
         grad_x = torch.empty_like(x32) if need_x else None
         grad_wp = torch.empty_like(wp32) if need_w else None
         grad_wn = torch.empty_like(wn32) if need_w else None
-        workspace = None
-        if need_w:
-            ws = _lib.backward_workspace_bytes(m, k, o, size)
-            workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=x32.device)
+        # The workspace holds the per-column output clusters as well as the dVth
+        # partials, so it is passed for dX-only calls too (same kernel, same bits).
+        ws = _lib.backward_workspace_bytes(m, k, o, size)
+        workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=x32.device)
         with torch.cuda.device(x32.device):
             _lib.backward(x32, wp32, wn32, g32, ctx.lut, size, dmin, scale, v_sat,
                           grad_x, grad_wp, grad_wn, workspace)
@@ -133,10 +133,8 @@ class LUTCudaEKVTIAFn(torch.autograd.Function):
             grad_x = torch.empty_like(x32) if need_x else None
             grad_wp = torch.empty_like(wp32) if need_w else None
             grad_wn = torch.empty_like(wn32) if need_w else None
-            ws = None
-            if need_w:
-                ws = torch.empty(max(_lib.backward_workspace_bytes(m, k, o, size), 16), dtype=torch.uint8,
-                                 device=x32.device)
+            ws = torch.empty(max(_lib.backward_workspace_bytes(m, k, o, size), 16), dtype=torch.uint8,
+                             device=x32.device)
             with torch.cuda.device(x32.device):
                 _lib.backward(x32, wp32, wn32, g_idiff, ctx.lut, size, dmin, scale, v_sat,
                               grad_x, grad_wp, grad_wn, ws)

@@ -52,9 +52,7 @@ def gpu_backward(x, wp, wn, g, lut, dmin, scale, size, v_sat=CFG_V_SAT, need_x=T
     gx = torch.full((m, k), float("nan"), device="cuda") if need_x else None
     gwp = torch.full((o, k), float("nan"), device="cuda") if need_w else None
     gwn = torch.full((o, k), float("nan"), device="cuda") if need_w else None
-    ws = None
-    if need_w:
-        ws = torch.empty(max(_lib.backward_workspace_bytes(m, k, o, size), 16), dtype=torch.uint8, device="cuda")
+    ws = torch.empty(max(_lib.backward_workspace_bytes(m, k, o, size), 16), dtype=torch.uint8, device="cuda")
     _lib.backward(xd, pd, nd, gd, lut, size, dmin, scale, v_sat, gx, gwp, gwn, ws)
     return tuple(None if t is None else t.cpu().numpy() for t in (gx, gwp, gwn))
 
@@ -314,3 +312,58 @@ def test_forward_ksplit_rows_match_unsplit_rows():
     assert_close_scaled(split[rows], ref, mag, what="split rows")
     _, mag_all = oracle.forward(x[:256], wp, wn, bf16_bits_to_f32(tib), dmin, scale, CFG_V_SAT, with_mag=True)
     assert_close_scaled(split[:256], whole[:256], mag_all, what="split vs unsplit")
+
+
+# Layers of 768..4096 outputs take the clustered backward (per-column output
+# clusters, g staged per token tile, interleaved table): ragged sizes (pads in
+# the last cluster, partial token tiles, column groups past K), both table
+# sizes, the clamped path, thresholds spread wider than a cluster window, and
+# the full-call / partial-call bits.
+CLUSTER_SHAPES = [(40, 5, 768), (129, 33, 1000), (300, 17, 2050), (77, 3, 4096)]
+
+
+@pytest.mark.parametrize("shape", CLUSTER_SHAPES)
+@pytest.mark.parametrize("size", [4096, 8192])
+def test_clustered_backward_matches_oracle(shape, size):
+    m, k, o = shape
+    rng = np.random.default_rng(m + 7 * k + o + size)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    wp = (2.5 + rng.uniform(-0.10712, 0.10712, (o, k))).astype(np.float32)
+    wn = (2.5 + rng.uniform(-0.10712, 0.10712, (o, k))).astype(np.float32)
+    g = rng.standard_normal((m, o)).astype(np.float32)
+    check_all(x, wp, wn, g, *cfg_tables(size), tag=f"clustered {shape} T={size}")
+
+
+@pytest.mark.parametrize("dist", ["clamp_both", "wide_thresholds"])
+def test_clustered_backward_edge_inputs(dist):
+    rng = np.random.default_rng(11)
+    m, k, o = 96, 9, 900
+    if dist == "clamp_both":  # dV beyond both table ends in every tile: clamped variant
+        x = (rng.standard_normal((m, k)) * 8).astype(np.float32)
+        wp = rng.uniform(0.0, 5.0, (o, k)).astype(np.float32)
+    else:  # thresholds over the whole [0, 5] range: clusters span many table entries
+        x = rng.uniform(0.0, 4.0, (m, k)).astype(np.float32)
+        wp = rng.uniform(0.0, 5.0, (o, k)).astype(np.float32)
+    wn = rng.uniform(0.0, 5.0, (o, k)).astype(np.float32)
+    g = rng.standard_normal((m, o)).astype(np.float32)
+    check_all(x, wp, wn, g, *cfg_tables(4096), tag=f"clustered {dist}")
+
+
+def test_clustered_backward_partial_calls_and_determinism():
+    tib, tdb, dmin, scale, size = cfg_tables(4096)
+    lut = pack(tib, tdb)
+    rng = np.random.default_rng(5)
+    m, k, o = 200, 21, 1100
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    wp = (2.5 + rng.uniform(-0.1, 0.1, (o, k))).astype(np.float32)
+    wn = (2.5 + rng.uniform(-0.1, 0.1, (o, k))).astype(np.float32)
+    g = rng.standard_normal((m, o)).astype(np.float32)
+    full = gpu_backward(x, wp, wn, g, lut, dmin, scale, size)
+    again = gpu_backward(x, wp, wn, g, lut, dmin, scale, size)
+    for a, b in zip(full, again):
+        np.testing.assert_array_equal(a, b)
+    only_x = gpu_backward(x, wp, wn, g, lut, dmin, scale, size, need_w=False)
+    only_w = gpu_backward(x, wp, wn, g, lut, dmin, scale, size, need_x=False)
+    np.testing.assert_array_equal(only_x[0], full[0])
+    np.testing.assert_array_equal(only_w[1], full[1])
+    np.testing.assert_array_equal(only_w[2], full[2])
