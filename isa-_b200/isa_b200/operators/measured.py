@@ -10,9 +10,13 @@ assignment are non-persistent buffers with the reference's names.
 
 The measured forward runs ``cimekv_measured_forward`` (per-cell coefficient
 gather, fused ``* r_tia`` and clamp) and its input gradient
-``cimekv_measured_backward_x``.  The piecewise-linear codebook is supported;
-the binned-input variant (``vin_lut_bins > 0``) is not, as in the reference's
-fused backend (``measured_deployment/fused_backend.py:46-56``).
+``cimekv_measured_backward_x``.  With ``vin_lut_bins > 0`` (binned inputs,
+``operator.py:99-110,176-188``) every input is first replaced by the centre of
+its bin with the reference's fp32 arithmetic, and the same kernel evaluates the
+measured curves there: that is the reference's per-bin difference current
+(``currents_at`` at the centre, pos minus neg device) summed over inputs.  As in
+the reference, the binned output carries no gradient to the input (the bin
+masks are not differentiable).
 """
 
 from __future__ import annotations
@@ -70,7 +74,7 @@ class DeploymentAwareCIMLinear(CIMLinear):
         self.vin_lut_bins = 0
         self.lookup_min = float(self.cfg.get("V_min", 0.0))
         self.lookup_max = float(self.cfg.get("V_max", 4.0))
-        for name in ("measured_vg", "measured_currents", "_coef"):
+        for name in ("measured_vg", "measured_currents", "_coef", "bin_centers", "diff_current"):
             self.register_buffer(name, torch.empty(0), persistent=False)
         self.register_buffer("pos_idx", torch.empty(0, dtype=torch.int16), persistent=False)
         self.register_buffer("neg_idx", torch.empty(0, dtype=torch.int16), persistent=False)
@@ -88,10 +92,8 @@ class DeploymentAwareCIMLinear(CIMLinear):
 
     @torch.no_grad()
     def configure_codebook(self, vg: torch.Tensor, currents_a: torch.Tensor, vin_lut_bins: int = 0) -> None:
-        """S measured curves ``currents_a[S, G]`` on the gate-voltage grid ``vg[G]``."""
-        if int(vin_lut_bins) != 0:
-            raise NotImplementedError("vin_lut_bins > 0 (binned inputs) is not supported; use the "
-                                      "piecewise-linear codebook (vin_lut_bins=0)")
+        """S measured curves ``currents_a[S, G]`` on the gate-voltage grid ``vg[G]``;
+        ``vin_lut_bins > 0`` bins the inputs (reference ``operator.py:88-110``)."""
         dev = self.vth_pos.device
         vg = vg.detach().to(device=dev, dtype=torch.float32).contiguous()
         cur = currents_a.detach().to(device=dev, dtype=torch.float32).contiguous()
@@ -103,7 +105,9 @@ class DeploymentAwareCIMLinear(CIMLinear):
         self.measured_currents = cur
         self.lookup_min = max(float(vg[0]), float(self.cfg.get("V_min", 0.0)))
         self.lookup_max = min(float(vg[-1]), float(self.cfg.get("V_max", 4.0)))
-        self.vin_lut_bins = 0
+        self.vin_lut_bins = int(vin_lut_bins)
+        if self.vin_lut_bins < 0:
+            raise ValueError("vin_lut_bins must be non-negative")
         # Per-segment slope and intercept of every curve, computed as in the
         # reference's set_assignment (operator.py:119-123).
         dv = vg[1:] - vg[:-1]
@@ -127,6 +131,33 @@ class DeploymentAwareCIMLinear(CIMLinear):
         if int(pos.max()) >= states or int(neg.max()) >= states:
             raise ValueError("Assignment references a state outside the codebook")
         self.pos_idx, self.neg_idx = pos, neg
+        if self.vin_lut_bins > 0:
+            # Bin centres and the per-bin difference currents, as the reference
+            # builds them (operator.py:99-110); the kernel evaluates the same
+            # curves at the centres instead of reading diff_current.
+            centers = torch.linspace(self.lookup_min, self.lookup_max, self.vin_lut_bins, device=dev,
+                                     dtype=torch.float32)
+            diff = torch.empty(self.vin_lut_bins, self.out_features, self.in_features, device=dev,
+                               dtype=torch.float32)
+            pl, nl = pos.long(), neg.long()
+            for b in range(self.vin_lut_bins):
+                cur = self.currents_at(centers[b])
+                diff[b] = cur[pl] - cur[nl]
+            self.bin_centers, self.diff_current = centers, diff
+        else:
+            self.bin_centers = torch.empty(0, device=dev)
+            self.diff_current = torch.empty(0, device=dev)
+
+    def _binned_inputs(self, x: torch.Tensor) -> torch.Tensor:
+        """Every input replaced by its bin centre, with the reference's fp32 ops
+        (clamp, (x - min) * (bins-1)/(max-min), round half to even, clamp)."""
+        flat = x.float().clamp(self.lookup_min, self.lookup_max)
+        if self.vin_lut_bins == 1:
+            ids = torch.zeros_like(flat, dtype=torch.long)
+        else:
+            scale = (self.vin_lut_bins - 1) / (self.lookup_max - self.lookup_min)
+            ids = torch.round((flat - self.lookup_min) * scale).long().clamp(0, self.vin_lut_bins - 1)
+        return self.bin_centers[ids]
 
     def currents_at(self, voltage) -> torch.Tensor:
         """All S curves evaluated at ``voltage`` (reference ``operator.py:147-161``)."""
@@ -145,6 +176,9 @@ class DeploymentAwareCIMLinear(CIMLinear):
             raise RuntimeError("Measured assignment is not initialized")
         if not x.is_cuda:
             raise RuntimeError("measured forward needs a CUDA tensor")
+        if self.vin_lut_bins > 0:
+            with torch.no_grad():  # bin masks: no gradient to the input (reference behaviour)
+                return _MeasuredFn.apply(self._binned_inputs(x.detach()), self).to(x.dtype)
         return _MeasuredFn.apply(x, self)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:

@@ -75,8 +75,8 @@ def test_measured_modes_and_unit_case():
     torch.testing.assert_close(y.detach(), layer(x).detach())
     y.sum().backward()
     assert layer.vth_pos.grad is not None  # gradient came from the continuous path
-    with pytest.raises(NotImplementedError):
-        layer.configure_codebook(torch.tensor([0.0, 1.0]), torch.tensor([[0.0, 1.0]]), vin_lut_bins=4)
+    with pytest.raises(ValueError):
+        layer.configure_codebook(torch.tensor([0.0, 1.0]), torch.tensor([[0.0, 1.0]]), vin_lut_bins=-1)
 
 
 @pytest.mark.gpu
@@ -118,3 +118,46 @@ def test_measured_kernels_random_shapes(shape, states, grid):
     assert_close_scaled(out.detach().cpu().numpy()[0], want, mag * r, what="measured out")
     gx_want, gmag = mref.backward_x(x, vg, currents, pos, neg, lmin, lmax, r, g)
     assert_close_scaled(xd.grad.cpu().numpy()[0], gx_want, gmag, what="measured grad_x")
+
+
+BINNED = ["measured_binned", "measured_binned_one", "measured_binned_ragged"]
+
+
+def _binned_args(g):
+    return (*_args(g), int(g["bins"]), g["bin_centers"])
+
+
+@pytest.mark.parametrize("case", BINNED)
+def test_oracle_matches_reference_binned_forward(case):
+    """Binned inputs (vin_lut_bins > 0): bin ids bit-exact, output at the suite's tolerance."""
+    g = load_golden(case)
+    out, _, mag = mref.forward_binned(g["x"], *_binned_args(g))
+    assert_close_scaled(out, g["out"], mag * float(g["r_tia"]), what=f"{case} out")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", BINNED)
+def test_binned_measured_forward_matches_reference(case):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from isa_b200.operators.measured import DeploymentAwareCIMLinear
+    g = load_golden(case)
+    m, k = g["x"].shape
+    o = g["pos"].shape[0]
+    layer = DeploymentAwareCIMLinear(k, o).cuda()
+    layer.set_r_tia(float(g["r_tia"]))
+    layer.configure_codebook(torch.from_numpy(g["vg"]), torch.from_numpy(g["currents"]), vin_lut_bins=int(g["bins"]))
+    layer.set_assignment(torch.from_numpy(g["pos"]), torch.from_numpy(g["neg"]))
+    layer.set_forward_mode("measured")
+    assert tuple(layer.diff_current.shape) == (int(g["bins"]), o, k)
+    x = torch.from_numpy(g["x"]).cuda().reshape(1, m, k).requires_grad_(True)
+    out = layer(x)
+    assert not out.requires_grad  # bin masks carry no input gradient, as in the reference
+    _, _, mag = mref.forward_binned(g["x"], *_binned_args(g))
+    assert_close_scaled(out.cpu().numpy()[0], g["out"], mag * float(g["r_tia"]), what=f"{case} out vs reference")
+    # STE mode: measured value, continuous gradient
+    layer.set_forward_mode("ste")
+    out_ste = layer(x)
+    assert_close_scaled(out_ste.detach().cpu().numpy()[0], g["out"], mag * float(g["r_tia"]), what="ste value")
+    out_ste.sum().backward()
+    assert x.grad is not None and bool(torch.isfinite(x.grad).all())
