@@ -33,7 +33,8 @@
 // interpolation are those of the unclustered kernel (lut_bwd2).
 
 constexpr int kCluMaxOutputs = 4096;  // outputs one column sort handles (o fits 13 key bits)
-constexpr int kCluMinOutputs = 768;   // below this the unclustered kernel is as fast (measured)
+constexpr int kCluMinOutputs = 768;        // T <= 4096: below this the unclustered kernel is as fast (measured)
+constexpr int kCluMinOutputsLargeT = 384;  // T > 4096
 constexpr int kB2Threads = 512;
 constexpr int kB2Warps = kB2Threads / 32;
 constexpr int kB2UMax = 24;  // clusters per warp (dVth sums in shared memory, [warp][cluster][lane])
@@ -354,7 +355,7 @@ __device__ __forceinline__ void b2_compute(const Bwd2Params& p, const LutConsts&
             v[0] += __shfl_xor_sync(0xffffffffu, v[0], s);
         }
     }
-    constexpr int kLog = kTM == 8 ? 3 : (kTM == 4 ? 2 : 1);
+    constexpr int kLog = kTM == 16 ? 4 : (kTM == 8 ? 3 : (kTM == 4 ? 2 : 1));
     if ((lane & ((1 << (5 - kLog)) - 1)) == 0) dxr_w[(lane >> (5 - kLog)) & (kTM - 1)] = v[0];
 }
 

@@ -1143,11 +1143,12 @@ int plan_backward(int M, int K, int O, int T, BwdPlan* plan, int stride = -1) {
 }
 
 // Plan of the clustered backward (bwd_cluster.cuh).  *ok = false when it does
-// not apply; the caller then runs bwd_kernel.  It applies from kCluMinOutputs
-// outputs up to kCluMaxOutputs, when tables + g tile fit shared memory.  Below
-// kCluMinOutputs the unclustered kernel measured as fast or faster (B200: 384
-// outputs 29.2 vs 30.4 ms, 256 outputs 14.8 vs 15.4 ms; at 768..3072 outputs
-// the clustered kernel is 3-14 % faster).
+// not apply; the caller then runs bwd_kernel.  It applies from
+// cluster_min_outputs(T) up to kCluMaxOutputs outputs, when tables + g tile fit
+// shared memory.  Below that the unclustered kernel measured as fast or faster
+// (B200, 32k tokens: T=4096 with 384 outputs 29.2 vs 30.4 ms, T=8192 with 256
+// outputs 14.8 vs 15.4 ms); the clustered one wins at 768..3072 outputs (3-14 %)
+// and at T=8192 from 384 outputs (32.7 -> 30.6 ms).
 struct Bwd2Plan {
     int kt, wpk, ncl, opad, tm, kgroups, tiles_m, nsplit, items, grid, sort_n, band;
     size_t smem, co_off, cr_off, part_off, workspace;
@@ -1164,9 +1165,22 @@ bool cluster_enabled() {
     return on;
 }
 
+// Smallest layer (outputs) the clustered kernel takes: kCluMinOutputs for
+// tables up to 4096 entries, kCluMinOutputsLargeT above (wider threshold
+// windows, more conflicts for the unclustered kernel).  CIMEKV_BWD_CLUSTER_MIN=<n>
+// in the environment overrides both (experiments).
+int cluster_min_outputs(int T) {
+    static const int v = [] {
+        const char* e = getenv("CIMEKV_BWD_CLUSTER_MIN");
+        return e ? atoi(e) : -1;
+    }();
+    if (v >= 0) return v;
+    return T > 4096 ? kCluMinOutputsLargeT : kCluMinOutputs;
+}
+
 int plan_backward2(int M, int K, int O, int T, Bwd2Plan* pl, bool* ok) {
     *ok = false;
-    if (!cluster_enabled() || O < kCluMinOutputs || O > kCluMaxOutputs || M <= 0 || K <= 0) return CIMEKV_OK;
+    if (!cluster_enabled() || O < cluster_min_outputs(T) || O > kCluMaxOutputs || M <= 0 || K <= 0) return CIMEKV_OK;
     int dev, sms, optin;
     int rc = current_device(&dev);
     if (rc || (rc = device_limits(dev, &sms, &optin))) return rc;
