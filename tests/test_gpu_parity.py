@@ -207,7 +207,8 @@ def test_partial_gradients_and_determinism():
         np.testing.assert_array_equal(gpu_forward(x, wp, wn, lut, dmin, scale, size), f1)
 
 
-def test_nan_inputs_follow_the_oracle():
+@pytest.mark.parametrize("o", [40, 800])  # 800 outputs: the clustered backward
+def test_nan_inputs_follow_the_oracle(o):
     """NaN inputs, as the reference's index rule and clamps treat them.
     A NaN threshold (wpos[5,2]) gives a NaN table coordinate, which the
     coordinate clamp (fminf/fmaxf, like tl.minimum/tl.maximum) turns into entry
@@ -220,7 +221,7 @@ def test_nan_inputs_follow_the_oracle():
     tib, tdb, dmin, scale, size = cfg_tables(4096)
     lut = pack(tib, tdb)
     rng = np.random.default_rng(5)
-    m, k, o = 70, 20, 40
+    m, k = 70, 20
     x = rng.standard_normal((m, k)).astype(np.float32)
     x[3, 7] = np.nan
     wp = (2.5 + rng.uniform(-0.1, 0.1, (o, k))).astype(np.float32)
