@@ -120,8 +120,7 @@ size_t cimekv_backward_workspace_bytes(int M, int K, int O, int table_size);
  * NULL (no threshold gradient).  The result is deterministic.
  * workspace: at least cimekv_backward_workspace_bytes(M, K, O, table_size)
  * bytes, 16-byte aligned.  It holds the per-token-split threshold partials
- * and, for layers of 768 (384 for tables above 4096 entries) to 4096
- * outputs, per input column the outputs
+ * and, for layers of 256 to 4096 outputs, per input column the outputs
  * regrouped into clusters of close thresholds (so the table gathers of a warp
  * hit distinct shared-memory banks).
  * A call with grad_wpos == grad_wneg == NULL may pass workspace = NULL; it then

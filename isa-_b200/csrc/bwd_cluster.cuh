@@ -20,7 +20,9 @@
 //
 // Work split: a persistent CTA (512 threads, one per SM) walks work items =
 // (group of kt input columns, token split).  Warp w serves column kk = w / wpk
-// and clusters cb, cb + wpk, ... (cb = w % wpk), at most kB2UMax of them.  Its
+// and clusters cb, cb + wpk, ... (cb = w % wpk); for layers with few outputs
+// (kt > 16) it serves whole columns w, w + 16, ... (cpw of them), so that every
+// warp has enough clusters per tile to amortise the tile's barrier and staging.  Its
 // dVth partial sums live in shared memory ([warp][cluster][lane], updated once
 // per cluster and tile, which keeps registers free for overlapping the
 // lookups) across all tiles of the item and go to the split's workspace slice
@@ -33,12 +35,13 @@
 // interpolation are those of the unclustered kernel (lut_bwd2).
 
 constexpr int kCluMaxOutputs = 4096;  // outputs one column sort handles (o fits 13 key bits)
-constexpr int kCluMinOutputs = 768;        // T <= 4096: below this the unclustered kernel is as fast (measured)
-constexpr int kCluMinOutputsLargeT = 384;  // T > 4096
+constexpr int kCluMinOutputs = 256;        // T <= 4096: smallest layer measured faster than the unclustered kernel
+constexpr int kCluMinOutputsLargeT = 256;  // T > 4096
 constexpr int kB2Threads = 512;
 constexpr int kB2Warps = kB2Threads / 32;
 constexpr int kB2UMax = 24;  // clusters per warp (dVth sums in shared memory, [warp][cluster][lane])
-constexpr int kB2MaxKT = 16;  // input columns per work item
+constexpr int kB2MaxKT = 32;  // input columns per work item
+constexpr int kB2MaxCpw = kB2MaxKT / kB2Warps;  // input columns one warp serves (layers with few outputs)
 
 // Unsigned key with the order of the fp32 values (negatives reversed).
 __device__ __forceinline__ uint32_t float_order_bits(float v) {
@@ -151,15 +154,15 @@ struct Bwd2Params {
     float* grad_x;
     float* part;  // [nsplit][2][O][K]
     int M, K, O, opad, T;
-    int kt, wpk, ncl, kgroups, tiles_m, nsplit, items;
+    int kt, wpk, cpw, ncl, kgroups, tiles_m, nsplit, items;  // cpw > 1 only with wpk == 1
     float dmin, scale, vsat;
 };
 
-__host__ __device__ inline size_t bwd2_smem_bytes(int stride, int tm, int opad, int kt) {
+__host__ __device__ inline size_t bwd2_smem_bytes(int stride, int tm, int opad, int kt, int cpw) {
     return (size_t)8 * stride                       // I and dI/dV pair tables
            + (size_t)2 * tm * opad * 4              // double-buffered g tile [tm/2][opad][2]
            + (size_t)2 * 3 * kt * tm * 4            // x, 1/d, -1/(v_sat d^2) per (column, token)
-           + (size_t)2 * kB2Warps * tm * 4          // per-warp dX sums
+           + (size_t)2 * kB2Warps * cpw * tm * 4    // per-(warp, column slot) dX sums
            + (size_t)2 * kB2Warps * sizeof(float4)   // x range per staging warp
            + (size_t)kB2Warps * kB2UMax * 32 * sizeof(float2);  // dVth sums per (warp, cluster, lane)
 }
@@ -256,7 +259,11 @@ __device__ __forceinline__ void b2_finish_dx(const Bwd2Params& p, int tile, int 
     const int m = tile * kTM + tt, k = k0 + kk;
     if (m >= p.M || k >= p.K) return;
     float s = 0.0f;
-    for (int c = 0; c < p.wpk; ++c) s += dxr[(b * kB2Warps + kk * p.wpk + c) * kTM + tt];
+    if (p.cpw == 1) {
+        for (int c = 0; c < p.wpk; ++c) s += dxr[(b * kB2Warps + kk * p.wpk + c) * kTM + tt];
+    } else {  // one warp per column: warp kk % kB2Warps, slot kk / kB2Warps
+        s = dxr[((b * kB2Warps + kk % kB2Warps) * p.cpw + kk / kB2Warps) * kTM + tt];
+    }
     p.grad_x[(int64_t)m * p.K + k] = s;
 }
 
@@ -365,8 +372,8 @@ __global__ void __launch_bounds__(kB2Threads, 1) bwd2_kernel(Bwd2Params p) {
     uint32_t* tab = reinterpret_cast<uint32_t*>(smem);                  // [kStride] I, [kStride] dI/dV
     float* gb = reinterpret_cast<float*>(smem + 8 * kStride);          // [2][kTM/2][opad][2]
     float* xb = gb + (size_t)2 * kTM * p.opad;                          // [2][3][kt][kTM]
-    float* dxr = xb + 2 * 3 * p.kt * kTM;                               // [2][kB2Warps][kTM]
-    float4* rng = reinterpret_cast<float4*>(dxr + 2 * kB2Warps * kTM);  // [2][kB2Warps]
+    float* dxr = xb + 2 * 3 * p.kt * kTM;                               // [2][kB2Warps][cpw][kTM]
+    float4* rng = reinterpret_cast<float4*>(dxr + 2 * kB2Warps * p.cpw * kTM);  // [2][kB2Warps]
     const int warp = threadIdx.x >> 5;
     float2* accw = reinterpret_cast<float2*>(rng + 2 * kB2Warps) + warp * kB2UMax * 32;  // this warp's dVth sums
 
@@ -387,7 +394,8 @@ __global__ void __launch_bounds__(kB2Threads, 1) bwd2_kernel(Bwd2Params p) {
     lc.inv = 0.0f;
     lc.vd = 0.0f;
 
-    const int kk_w = warp / p.wpk, cb = warp - kk_w * p.wpk;
+    const int kk_w = warp / p.wpk, cb = warp - kk_w * p.wpk;  // column slot 0; slot cs adds cs * kB2Warps
+    const int slot_units = (p.ncl + p.wpk - 1) / p.wpk;        // accumulator slots per column slot
     const int nslots = (p.kt * kTM + 31) >> 5;
     const uint32_t gb_s = smem_u32addr(gb);
     int buf = 0;
@@ -404,7 +412,6 @@ __global__ void __launch_bounds__(kB2Threads, 1) bwd2_kernel(Bwd2Params p) {
             wmax = fmaxf(wmax, r.y);
             wnan |= r.z != 0.0f;
         }
-        const int k = k0 + kk_w;
         for (int s = 0; s < kB2UMax; ++s) accw[s * 32 + (threadIdx.x & 31)] = make_float2(0.0f, 0.0f);
 
         float xnext = 0.0f;  // x of the tile after the next one to stage
@@ -429,30 +436,34 @@ __global__ void __launch_bounds__(kB2Threads, 1) bwd2_kernel(Bwd2Params p) {
                 xr.y = fmaxf(xr.y, q.y);
                 xr.z = fmaxf(xr.z, q.z);
             }
-            if (k < p.K) {
-                const bool fast = tile_in_table(xr.x, xr.y, wmin, wmax, wnan || xr.z != 0.0f, p.dmin, p.scale, p.T);
-                const uint32_t gt = gb_s + (uint32_t)(buf * kTM * p.opad * 4);
-                const float* xs = xb + (size_t)buf * 3 * p.kt * kTM;
-                float* dxr_w = dxr + (buf * kB2Warps + warp) * kTM;
+            const bool fast = tile_in_table(xr.x, xr.y, wmin, wmax, wnan || xr.z != 0.0f, p.dmin, p.scale, p.T);
+            const uint32_t gt = gb_s + (uint32_t)(buf * kTM * p.opad * 4);
+            const float* xs = xb + (size_t)buf * 3 * p.kt * kTM;
+            for (int cs = 0; cs < p.cpw; ++cs) {
+                const int kk = kk_w + cs * kB2Warps, k = k0 + kk;
+                if (k >= p.K) break;
+                float* dxr_w = dxr + ((buf * kB2Warps + warp) * p.cpw + cs) * kTM;
+                float2* acc_cs = accw + cs * slot_units * 32;
                 if (fast) {
-                    b2_compute<false, kStride, kTM>(p, lc, k, kk_w, cb, gt, xs, accw, dxr_w);
+                    b2_compute<false, kStride, kTM>(p, lc, k, kk, cb, gt, xs, acc_cs, dxr_w);
                 } else {
-                    b2_compute<true, kStride, kTM>(p, lc, k, kk_w, cb, gt, xs, accw, dxr_w);
+                    b2_compute<true, kStride, kTM>(p, lc, k, kk, cb, gt, xs, acc_cs, dxr_w);
                 }
             }
             buf ^= 1;
         }
         __syncthreads();  // last tile's dX slots complete
         if (tlo < thi) b2_finish_dx<kTM>(p, thi - 1, buf ^ 1, k0, dxr);
-        if (p.part != nullptr && k < p.K) {
+        for (int cs = 0; p.part != nullptr && cs < p.cpw; ++cs) {
+            const int k = k0 + kk_w + cs * kB2Warps;
+            if (k >= p.K) break;
             const int lane = threadIdx.x & 31;
-#pragma unroll
-            for (int s = 0; s < kB2UMax; ++s) {
+            for (int s = 0; s < slot_units; ++s) {
                 const int cl = cb + s * p.wpk;
                 if (cl < p.ncl) {
                     const int o = __ldg(p.co + (int64_t)k * p.opad + cl * 32 + lane);
                     if (o < p.O) {
-                        const float2 v = accw[s * 32 + lane];
+                        const float2 v = accw[(cs * slot_units + s) * 32 + lane];
                         p.part[(((int64_t)split * 2 + 0) * p.O + o) * p.K + k] = v.x;
                         p.part[(((int64_t)split * 2 + 1) * p.O + o) * p.K + k] = v.y;
                     }

@@ -1145,12 +1145,13 @@ int plan_backward(int M, int K, int O, int T, BwdPlan* plan, int stride = -1) {
 // Plan of the clustered backward (bwd_cluster.cuh).  *ok = false when it does
 // not apply; the caller then runs bwd_kernel.  It applies from
 // cluster_min_outputs(T) up to kCluMaxOutputs outputs, when tables + g tile fit
-// shared memory.  Below that the unclustered kernel measured as fast or faster
-// (B200, 32k tokens: T=4096 with 384 outputs 29.2 vs 30.4 ms, T=8192 with 256
-// outputs 14.8 vs 15.4 ms); the clustered one wins at 768..3072 outputs (3-14 %)
-// and at T=8192 from 384 outputs (32.7 -> 30.6 ms).
+// shared memory.  Measured on B200 at 32k tokens against the unclustered
+// kernel: 384 outputs T=4096 28.0-28.6 vs 29.2 ms, 384 outputs T=8192 28.3-29.0
+// vs 32.7 ms, 256 outputs T=8192 14.0-14.2 vs 14.8 ms (two columns per warp),
+// 768..3072 outputs 3-14 % faster; smaller layers are not measured and keep
+// the unclustered kernel.
 struct Bwd2Plan {
-    int kt, wpk, ncl, opad, tm, kgroups, tiles_m, nsplit, items, grid, sort_n, band;
+    int kt, wpk, cpw, ncl, opad, tm, kgroups, tiles_m, nsplit, items, grid, sort_n, band;
     size_t smem, co_off, cr_off, part_off, workspace;
 };
 
@@ -1189,17 +1190,26 @@ int plan_backward2(int M, int K, int O, int T, Bwd2Plan* pl, bool* ok) {
     pl->opad = pl->ncl * 32;
     int kmax = 1;
     while (kmax < K && kmax < kB2MaxKT) kmax <<= 1;
+    // Largest column group whose clusters fit kB2UMax per warp: kt <= 16 columns
+    // share the 16 warps (wpk warps per column); kt = 32 gives each warp two
+    // whole columns (layers of up to 12 clusters, i.e. 384 outputs).
     for (pl->kt = kmax; pl->kt >= 1; pl->kt >>= 1) {
-        if (kB2Warps % pl->kt) continue;
-        pl->wpk = kB2Warps / pl->kt;
-        if ((pl->ncl + pl->wpk - 1) / pl->wpk <= kB2UMax) break;
+        if (pl->kt > kB2Warps) {
+            pl->cpw = pl->kt / kB2Warps;
+            pl->wpk = 1;
+        } else {
+            if (kB2Warps % pl->kt) continue;
+            pl->cpw = 1;
+            pl->wpk = kB2Warps / pl->kt;
+        }
+        if ((pl->ncl + pl->wpk - 1) / pl->wpk * pl->cpw <= kB2UMax) break;
     }
     if (pl->kt < 1) return CIMEKV_OK;
     pl->tm = 8;
-    pl->smem = bwd2_smem_bytes(stride, 8, pl->opad, pl->kt);
+    pl->smem = bwd2_smem_bytes(stride, 8, pl->opad, pl->kt, pl->cpw);
     if (pl->smem > (size_t)optin) {
         pl->tm = 4;
-        pl->smem = bwd2_smem_bytes(stride, 4, pl->opad, pl->kt);
+        pl->smem = bwd2_smem_bytes(stride, 4, pl->opad, pl->kt, pl->cpw);
     }
     if (pl->smem > (size_t)optin) return CIMEKV_OK;
     pl->kgroups = (K + pl->kt - 1) / pl->kt;
@@ -1261,6 +1271,7 @@ int launch_backward2_stride(const Bwd2Plan& pl, int dev, int optin, const float*
     p.T = T;
     p.kt = pl.kt;
     p.wpk = pl.wpk;
+    p.cpw = pl.cpw;
     p.ncl = pl.ncl;
     p.kgroups = pl.kgroups;
     p.tiles_m = pl.tiles_m;

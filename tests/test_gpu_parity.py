@@ -320,7 +320,7 @@ def test_forward_ksplit_rows_match_unsplit_rows():
 # the last cluster, partial token tiles, column groups past K), both table
 # sizes, the clamped path, thresholds spread wider than a cluster window, and
 # the full-call / partial-call bits.
-CLUSTER_SHAPES = [(40, 5, 768), (129, 33, 1000), (300, 17, 2050), (77, 3, 4096), (50, 11, 400)]
+CLUSTER_SHAPES = [(40, 5, 768), (129, 33, 1000), (300, 17, 2050), (77, 3, 4096), (50, 11, 400), (60, 45, 384)]
 
 
 @pytest.mark.parametrize("shape", CLUSTER_SHAPES)
