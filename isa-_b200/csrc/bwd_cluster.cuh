@@ -439,15 +439,27 @@ __global__ void __launch_bounds__(kB2Threads, 1) bwd2_kernel(Bwd2Params p) {
             const bool fast = tile_in_table(xr.x, xr.y, wmin, wmax, wnan || xr.z != 0.0f, p.dmin, p.scale, p.T);
             const uint32_t gt = gb_s + (uint32_t)(buf * kTM * p.opad * 4);
             const float* xs = xb + (size_t)buf * 3 * p.kt * kTM;
-            for (int cs = 0; cs < p.cpw; ++cs) {
-                const int kk = kk_w + cs * kB2Warps, k = k0 + kk;
-                if (k >= p.K) break;
-                float* dxr_w = dxr + ((buf * kB2Warps + warp) * p.cpw + cs) * kTM;
-                float2* acc_cs = accw + cs * slot_units * 32;
-                if (fast) {
-                    b2_compute<false, kStride, kTM>(p, lc, k, kk, cb, gt, xs, acc_cs, dxr_w);
-                } else {
-                    b2_compute<true, kStride, kTM>(p, lc, k, kk, cb, gt, xs, acc_cs, dxr_w);
+            if (p.cpw == 1) {  // straight-line path (a runtime slot loop here measured 6 % slower at 4-token tiles)
+                const int k = k0 + kk_w;
+                if (k < p.K) {
+                    float* dxr_w = dxr + (buf * kB2Warps + warp) * kTM;
+                    if (fast) {
+                        b2_compute<false, kStride, kTM>(p, lc, k, kk_w, cb, gt, xs, accw, dxr_w);
+                    } else {
+                        b2_compute<true, kStride, kTM>(p, lc, k, kk_w, cb, gt, xs, accw, dxr_w);
+                    }
+                }
+            } else {
+                for (int cs = 0; cs < p.cpw; ++cs) {
+                    const int kk = kk_w + cs * kB2Warps, k = k0 + kk;
+                    if (k >= p.K) break;
+                    float* dxr_w = dxr + ((buf * kB2Warps + warp) * p.cpw + cs) * kTM;
+                    float2* acc_cs = accw + cs * slot_units * 32;
+                    if (fast) {
+                        b2_compute<false, kStride, kTM>(p, lc, k, kk, cb, gt, xs, acc_cs, dxr_w);
+                    } else {
+                        b2_compute<true, kStride, kTM>(p, lc, k, kk, cb, gt, xs, acc_cs, dxr_w);
+                    }
                 }
             }
             buf ^= 1;
