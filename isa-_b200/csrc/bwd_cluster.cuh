@@ -29,8 +29,8 @@
 // once at the end (reduced in a fixed order by bwd_reduce_kernel).  The
 // thresholds and output index of the next cluster are fetched while the
 // current one runs; the table is staged as interleaved {I pair, dI pair}
-// words, so one 64-bit shared load serves a lookup.  Per kTM-token tile a warp sums its dX partials over
-// lanes by a butterfly; the warps of one column add theirs in a fixed order
+// words, so one 64-bit shared load serves a lookup.  Per kTM-token tile a warp
+// sums its dX partials over lanes by a butterfly; the warps of one column add theirs in a fixed order
 // after the next tile's barrier.  The cell arithmetic, index rule and
 // interpolation are those of the unclustered kernel (lut_bwd2).
 
@@ -40,8 +40,7 @@ constexpr int kCluMinOutputsLargeT = 256;  // T > 4096
 constexpr int kB2Threads = 512;
 constexpr int kB2Warps = kB2Threads / 32;
 constexpr int kB2UMax = 24;  // clusters per warp (dVth sums in shared memory, [warp][cluster][lane])
-constexpr int kB2MaxKT = 32;  // input columns per work item
-constexpr int kB2MaxCpw = kB2MaxKT / kB2Warps;  // input columns one warp serves (layers with few outputs)
+constexpr int kB2MaxKT = 32;  // input columns per work item (two per warp for layers of <= 12 clusters)
 
 // Unsigned key with the order of the fp32 values (negatives reversed).
 __device__ __forceinline__ uint32_t float_order_bits(float v) {
@@ -178,8 +177,6 @@ __device__ __forceinline__ f32x2 lds64(uint32_t addr) {
     asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(addr));
     return v;
 }
-
-
 
 // Backward lookup pair from the interleaved table {I pair word, dI pair word}
 // (8 bytes per entry; tab_base is pre-offset by -(2^23 bits) * 8).
