@@ -300,7 +300,7 @@ __device__ __forceinline__ void b2_compute(const Bwd2Params& p, const LutConsts&
         w_next = __ldg(cwk + cb * 32 + lane);
         o_next = __ldg(cok + cb * 32 + lane);
     }
-#pragma unroll 2
+#pragma unroll 3
     for (int s = 0; s < nun; ++s) {
         {
             f32x2 ua = pk2(0.0f, 0.0f), un = pk2(0.0f, 0.0f);
